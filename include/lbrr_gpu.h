@@ -1,0 +1,178 @@
+/*
+ * lbrr_gpu.h -- C ABI of the B200 (sm_100a) BS-RoFormer engine.
+ *
+ * Drop-in for the GPU pipeline of logic-bs-roformer-rs (`lbrr`): everything
+ * src/main.rs does from `CudaContext::new` to the device-to-host copy of the
+ * separated stems, i.e. upload_weights (src/main.rs:6045-6077),
+ * bench_forward + transformer_step (:7014-7162, :6131-6268), istft_ola
+ * (:5024-5039) and the song loop with ola_demix (:7598-7775, :5052-5123).
+ *
+ * Conventions (modelled on the reference's own C shim,
+ * tools/cudnn_sdpa_wrap.cpp:149-168, :226-244): opaque handles, int status
+ * (0 = OK, negative = error), a thread-local last-error string, all device
+ * work ordered on one stream per engine.  No function aborts or exits.
+ * Plain pointers and sizes only; `stream` is a cudaStream_t passed as void*.
+ *
+ * Layouts at the boundary (src/main.rs:7283, :7739, src/benchmark.rs:93):
+ *   input audio   interleaved stereo fp32 [len][2]
+ *   output stems  planar fp32 [6][2][len], stem order of the model YAML
+ *                 (bass, drums, other, vocals, guitar, piano)
+ * fp16 tensors of the per-op entry points are IEEE binary16 bit patterns
+ * (uint16_t), row-major.
+ */
+#ifndef LBRR_GPU_H
+#define LBRR_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LBRR_OK 0
+#define LBRR_ERR_INVALID (-1)       /* bad argument / shape / configuration           */
+#define LBRR_ERR_CUDA (-2)          /* a CUDA runtime or cuFFT call failed             */
+#define LBRR_ERR_WEIGHTS (-3)       /* checkpoint validation failed                    */
+#define LBRR_ERR_DEVICE (-4)        /* a kernel reported a status (wait timeout, ...)  */
+#define LBRR_ERR_STATE (-5)         /* call out of order (e.g. forward before weights) */
+#define LBRR_ERR_PEER (-6)          /* multi-GPU stitching failed                      */
+
+typedef struct lbrr_engine lbrr_engine;
+
+/* Model hyper-parameters; replaces config.rs ModelConfig (src/config.rs:92-133).
+ * The engine supports exactly the BS-RoFormer geometry of
+ * assets/logic_bs_roformer.yaml and rejects anything else with LBRR_ERR_INVALID. */
+typedef struct lbrr_model_desc {
+  int32_t dim;            /* 256  */
+  int32_t depth;          /* 12   */
+  int32_t heads;          /* 8    */
+  int32_t dim_head;       /* 64   */
+  int32_t num_stems;      /* 6    */
+  int32_t mlp_expansion;  /* 4    */
+  int32_t n_fft;          /* 2048 */
+  int32_t hop;            /* 512  */
+  int32_t sample_rate;    /* 44100 */
+  int32_t num_bands;      /* 62   */
+  const int32_t* freqs_per_band; /* num_bands entries, sum 1025 */
+} lbrr_model_desc;
+
+/* One fp32 checkpoint tensor, keyed by its safetensors name (src/weights.rs:41-55). */
+typedef struct lbrr_weight_view {
+  const char* name;
+  const float* data;      /* host memory, row-major as stored in the checkpoint */
+  int64_t numel;
+} lbrr_weight_view;
+
+/* Song chunking (src/main.rs:7617-7619): chunk 588800, step 559360, border 29440. */
+typedef struct lbrr_chunk_plan {
+  int64_t chunk;
+  int64_t step;
+  int64_t border;
+} lbrr_chunk_plan;
+
+/* Last error message of the calling thread (replaces wrap_last_error,
+ * tools/cudnn_sdpa_wrap.cpp:68, :244).  Never NULL. */
+const char* lbrr_last_error(void);
+
+/* ABI version: 1. */
+int lbrr_abi_version(void);
+
+/* Fill `desc` with the supported model (assets/logic_bs_roformer.yaml:11-84).
+ * `freqs_out` receives num_bands (62) entries and is referenced by desc. */
+int lbrr_default_model(lbrr_model_desc* desc, int32_t* freqs_out, int32_t capacity);
+
+/* Create an engine on `device` with scratch sized for chunks of up to
+ * max_chunk_samples stereo samples (replaces CudaContext::new + make_bench_bufs +
+ * RuntimeScratch::new, src/main.rs:7645-7684, :7169-7197, :5995-6002). */
+int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64_t max_chunk_samples, lbrr_engine** out);
+
+/* Validate and upload a checkpoint (replaces ModelWeights::load + upload_weights,
+ * src/weights.rs:307-447, src/main.rs:6045-6077): every one of the 1989 keys
+ * exactly once with its exact size, per-layer qkv/out biases bit-equal to
+ * linear_62_bias_0 / linear_64_bias_0, rotary freqs = 1/10000^(2i/64).
+ * GEMM weights are rounded to fp16 (RNE, the src/fp16.rs bit contract). */
+int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size_t n);
+
+/* Same, reading a .safetensors file (F32 tensors; src/weights.rs:25-55). */
+int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path);
+
+/* One chunk, device buffers on the engine's device, stream-ordered on `stream`
+ * (NULL = the engine's stream).  x_dev: [len][2] fp32, stems_dev: [6][2][len]
+ * fp32.  len must satisfy n_fft/2 < len <= max_chunk_samples (src/main.rs:7263).
+ * Replaces bench_forward + istft_ola (src/main.rs:7014-7162, :7303-7306). */
+int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);
+
+/* End to end from host memory: stage x_host through pinned memory, copy to
+ * the device, forward, copy the stems back, synchronise, check the device
+ * status.  x_host: [len][2], stems_host: [6][2][len]. */
+int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, float* stems_host);
+
+/* Front end and the first n_steps transformer axes only (n_steps in 0..24;
+ * 0 = band-split output); writes the folded token tensor x[T*62][256] fp32
+ * to x_out_dev.  Diagnostic stage boundary of the same pipeline
+ * (the reference's --dump-trunk taps, src/main.rs:7055-7092). */
+int lbrr_forward_trunk(lbrr_engine* e, const float* x_dev, int64_t len, int n_steps, float* x_out_dev,
+                       void* stream);
+
+/* Synchronise the engine stream and check the device status word. */
+int lbrr_engine_sync(lbrr_engine* e);
+
+/* Resident bytes: weights and scratch (src/main.rs:7199-7252). */
+int lbrr_engine_memory(const lbrr_engine* e, int64_t* weight_bytes, int64_t* scratch_bytes);
+
+void lbrr_engine_destroy(lbrr_engine* e);
+
+/* Whole song (replaces separate()'s GPU loop, src/main.rs:7617-7775): reflect
+ * pad, chunk grid, per-chunk forward, fade-weighted overlap-add, division by
+ * the fade energy, crop.  Chunks are dealt round-robin over the n_engines
+ * engines (one per GPU, one host thread each); every chunk's ISTFT waveform
+ * is copied peer-to-peer to engines[0]'s device and accumulated there in
+ * chunk order, so the result does not depend on n_engines.
+ * host_interleaved: [len][2]; host_out: [6][2][len]. */
+int lbrr_separate_song(lbrr_engine* const* engines, int n_engines, const float* host_interleaved, int64_t len,
+                       const lbrr_chunk_plan* plan, float* host_out);
+
+/* ---------------------------------------------------------------------------
+ * Per-op entry points (device pointers, fp16 as uint16_t bits).  Each mirrors
+ * one kernel or library call of transformer_step / bench_forward and exists so
+ * the pieces can be checked and timed on their own.  All are asynchronous on
+ * `stream`; lbrr_op_sync() synchronises it and checks the per-device status.
+ * ------------------------------------------------------------------------- */
+
+/* rmsnorm_gates_h16 (src/main.rs:616-703): h16[rows][256], gates[rows][8]. */
+int lbrr_op_norm_gates(const float* x, const float* gamma, const float* gate_w, const float* gate_b, uint16_t* h16,
+                       float* gates, int64_t rows, void* stream);
+
+/* QKV GEMM + shared bias (fp16) + RoPE on Q and K (cuBLASLt matmul_f16out +
+ * rope_q16_inplace + rope_k16, src/main.rs:6157-6187).  h16[M][256],
+ * w16[1536][256], bias16[1536] (fp32 values already rounded to fp16),
+ * cos/sin[P][32] with P = frames (axis 0) or bands (axis 1), qkv[M][1536],
+ * M = frames * bands, token = t*bands + b. */
+int lbrr_op_qkv_rope(const uint16_t* h16, const uint16_t* w16, const float* bias16, const float* cos_tab,
+                     const float* sin_tab, uint16_t* qkv, int64_t frames, int32_t bands, int32_t axis, void* stream);
+
+/* Gated SDPA over one axis (CudnnSdpa::execute + sdpa_gate,
+ * src/main.rs:6193-6199): out[M][512] = f16(f16(softmax(QK^T/8) V) * sigmoid(gate)). */
+int lbrr_op_attention(const uint16_t* qkv, const float* gates, uint16_t* out, int64_t frames, int32_t bands,
+                      int32_t axis, void* stream);
+
+/* Out-projection + bias + residual, fused with the pre-FF RMSNorm
+ * (matmul_resid + rmsnorm_h16, src/main.rs:6219-6234). */
+int lbrr_op_outproj_norm(const uint16_t* scaled16, const uint16_t* w16, const float* bias, const float* resid,
+                         const float* gamma, float* attn_out, uint16_t* h16, int64_t rows, void* stream);
+
+/* FF1 + A&S-erf GELU, fp16 out (gemm_f16_gelu_a16w, src/main.rs:2827-2949). */
+int lbrr_op_ff1_gelu(const uint16_t* h16, const uint16_t* w16, const float* b1, uint16_t* ff1, int64_t rows,
+                     void* stream);
+
+/* FF2 + bias + residual (matmul_resid, src/main.rs:6255-6259). */
+int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const float* b2, const float* resid, float* x,
+                      int64_t rows, void* stream);
+
+int lbrr_op_sync(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LBRR_GPU_H */

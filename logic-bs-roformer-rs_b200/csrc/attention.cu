@@ -1,0 +1,322 @@
+// Fused RoPE'd multi-head attention for both RoFormer axes on tcgen05.
+//
+// Replaces cuDNN SDPA + sdpa_gate of the reference (src/main.rs:6181-6199) and
+// its hand-written fallbacks attn_flash_tc / attn_flash_async (:3796-4312).
+// Q and K arrive already rotated (the QKV GEMM epilogue applies RoPE), V raw,
+// all inside the folded qkv tensor [M][1536] fp16 (token = t*nb + b).
+//
+// One CTA owns 128 query rows of one (sequence, head):
+//   time axis  sequence = band b, keys = all T frames (TMA 3-D box gathers the
+//              rows t*nb + b), key tiles of 128, online softmax;
+//   freq axis  two sequences (frames 2p, 2p+1) of nb = 62 bands packed into
+//              one 128-row tile (block-diagonal mask), a single key tile.
+// Pipeline (192 threads): warp 0 TMA (Q once, K/V double-buffered), warp 1
+// issues S = Q K^T (TMEM cols 0..127) and O += P V (TMEM cols 128..191, V as an
+// MN-major operand), warps 2..5 run the softmax with one query row per thread,
+// write P (fp16, 128-byte swizzled K-major) to shared memory, rescale O in
+// TMEM, and finally write f16(f16(O/l) * sigmoid(gate)).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lbrr {
+
+namespace {
+constexpr int kTile = 16384;  // one [128][64] fp16 tile
+constexpr int kOffQ = 0;
+constexpr int kOffK = kTile;
+constexpr int kOffV = 3 * kTile;
+constexpr int kOffP = 5 * kTile;
+constexpr int kOffBar = 7 * kTile;
+constexpr int kAttnSmem = kOffBar + 128;
+constexpr int kAttnThreads = 192;
+constexpr uint32_t kAttnTmemCols = 256;
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColO = 128;
+
+struct AttnArgs {
+  const float* gates;  // [M][8]
+  __half* out;         // [M][512]
+  int T, nb, axis, nk;
+  int* status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attn_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 6;
+  uint64_t* pv_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) report_status(a.status, kDevSmemMisaligned);
+    return;
+  }
+  const int nb = a.nb, T = a.T, nk = a.nk;
+  const bool time_axis = a.axis == 0;
+  const int head = time_axis ? (blockIdx.y & 7) : blockIdx.y;
+  const int band = time_axis ? (blockIdx.y >> 3) : 0;
+  const int qt = blockIdx.x;  // query tile (time) or sequence pair (freq)
+  const int row0 = qt * 2 * nb;  // freq axis: first token of the pair
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(&kv_full[0], 1);
+    mbar_init(&kv_full[1], 1);
+    mbar_init(&kv_empty[0], 1);
+    mbar_init(&kv_empty[1], 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch(&tm);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kAttnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kTile);
+      if (time_axis)
+        tma_load_3d(smem + kOffQ, &tm, q_full, head * 64, band, qt * 128);
+      else
+        tma_load_2d(smem + kOffQ, &tm, q_full, head * 64, row0);
+      for (int j = 0; j < nk; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, abort_flag, a.status)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 2 * kTile);
+        if (time_axis) {
+          tma_load_3d(smem + kOffK + s * kTile, &tm, &kv_full[s], 512 + head * 64, band, j * 128);
+          tma_load_3d(smem + kOffV + s * kTile, &tm, &kv_full[s], 1024 + head * 64, band, j * 128);
+        } else {
+          tma_load_2d(smem + kOffK + s * kTile, &tm, &kv_full[s], 512 + head * 64, row0);
+          tma_load_2d(smem + kOffV + s * kTile, &tm, &kv_full[s], 1024 + head * 64, row0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16_f32(128, 128);
+      const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
+      const uint32_t sq = smem_u32(smem + kOffQ);
+      auto issue_s = [&](int s) {
+        const uint32_t sk = smem_u32(smem + kOffK + s * kTile);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f16_ss(tmem + kColS, sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
+                     k > 0 ? 1u : 0u);
+      };
+      auto issue_pv = [&](int s, bool acc) {
+        const uint32_t sp = smem_u32(smem + kOffP);
+        const uint32_t sv = smem_u32(smem + kOffV + s * kTile);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ss(tmem + kColO, sdesc_sw128(sp + (kk >> 2) * kTile + (kk & 3) * 32, 1024, 16),
+                     sdesc_sw128(sv + kk * 2048, 1024, 0), id_o, (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag, a.status);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        mma_commit(s_full);
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        ok = mbar_wait(p_full, j & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (j + 1 < nk) {
+          const int s1 = (j + 1) & 1;
+          ok = mbar_wait(&kv_full[s1], ((j + 1) >> 1) & 1, abort_flag, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(s1);
+          mma_commit(s_full);
+        }
+        issue_pv(j & 1, j > 0);
+        mma_commit(pv_done);
+        mma_commit(&kv_empty[j & 1]);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue (one query row per thread) ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t tS = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColS;
+    const uint32_t tO = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColO;
+    const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
+    const int rseq = r / nb;                        // freq axis: which packed sequence
+    uint8_t* sP = smem + kOffP;
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      ok = mbar_wait(s_full, j & 1, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      const int key0 = j * 128;
+      auto key_ok = [&](int c) { return time_axis ? (key0 + c < T) : (c / nb == rseq); };
+      float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tS + c, v);
+        tmem_ld_wait(v);
+#pragma unroll
+        for (int k = 0; k < 32; ++k)
+          if (key_ok(c + k)) mx = fmaxf(mx, __uint_as_float(v[k]));
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float corr = ex2((m_run - m_use) * sc);
+      const float msc = m_use * sc;
+      if (j > 0) {
+        // PV_{j-1} must be done before O is rescaled and P is overwritten
+        ok = mbar_wait(pv_done, (j - 1) & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tO + c, v);
+            tmem_ld_wait(v);
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = __float_as_uint(__uint_as_float(v[k]) * corr);
+            tmem_st32(tO + c, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 128; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tS + c, v);
+        tmem_ld_wait(v);
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float p0 = key_ok(c + 2 * k) ? ex2(__uint_as_float(v[2 * k]) * sc - msc) : 0.f;
+          const float p1 = key_ok(c + 2 * k + 1) ? ex2(__uint_as_float(v[2 * k + 1]) * sc - msc) : 0.f;
+          sum += p0 + p1;
+          w[k] = pack_f16x2(p0, p1);
+        }
+        // row r of the K-major [128 rows][128 keys] P operand: key block c/64,
+        // 16-byte chunk ((c%64)/8 + i) swizzled with (r & 7)
+        uint8_t* base = sP + (c >> 6) * kTile + r * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int chunk = ((c & 63) >> 3) + i;
+          *reinterpret_cast<uint4*>(base + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+      l_run = l_run * corr + sum;
+      m_run = m_new;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok) ok = mbar_wait(pv_done, (nk - 1) & 1, abort_flag, a.status);
+    tc_fence_after();
+    if (ok && !*abort_flag) {
+      bool valid;
+      int token;
+      if (time_axis) {
+        const int qi = qt * 128 + r;
+        valid = qi < T;
+        token = qi * nb + band;
+      } else {
+        const int t = qt * 2 + rseq;
+        valid = r < 2 * nb && t < T;
+        token = t * nb + (r - rseq * nb);
+      }
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      float sig = 0.f;
+      if (valid) sig = 1.0f / (1.0f + __expf(-__ldg(a.gates + static_cast<size_t>(token) * 8 + head)));
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tO + c, v);
+        tmem_ld_wait(v);
+        if (!valid) continue;
+        uint32_t w[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float o0 = f16_round(__uint_as_float(v[2 * k]) * inv);
+          const float o1 = f16_round(__uint_as_float(v[2 * k + 1]) * inv);
+          w[k] = pack_f16x2(o0 * sig, o1 * sig);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(token) * 512 + head * 64 + c);
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
+        dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kAttnTmemCols);
+  }
+}
+}  // namespace
+
+cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
+                          cudaStream_t st) {
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  if (T <= 0) return cudaSuccess;
+  if (axis == 1 && 2 * nb > 128) return cudaErrorInvalidValue;  // two sequences per 128-row tile
+  CUtensorMap tm;
+  cudaError_t e;
+  AttnArgs a;
+  a.gates = gates;
+  a.out = out;
+  a.T = T;
+  a.nb = nb;
+  a.axis = axis;
+  a.status = status;
+  dim3 grid;
+  if (axis == 0) {
+    e = make_map_3d(&tm, qkv, 1536, nb, T, 1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
+    a.nk = (T + 127) / 128;
+    grid = dim3((T + 127) / 128, nb * 8);
+  } else {
+    e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
+    a.nk = 1;
+    grid = dim3((T + 1) / 2, 8);
+  }
+  if (e != cudaSuccess) return e;
+  attn_kernel<<<grid, kAttnThreads, kAttnSmem, st>>>(tm, a);
+  return cudaGetLastError();
+}
+
+}  // namespace lbrr

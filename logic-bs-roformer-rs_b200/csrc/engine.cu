@@ -1,0 +1,1057 @@
+// Engine and C ABI (include/lbrr_gpu.h): weight validation and placement,
+// per-length setup (RoPE tables, grouped-GEMM tile tables, cuFFT plans, ISTFT
+// envelope), the chunk forward, the whole-song overlap-add across engines and
+// the per-op entry points.
+#include <cufft.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/lbrr_gpu.h"
+#include "common.cuh"
+#include "kernels.h"
+
+using namespace lbrr;
+
+// ---------------------------------------------------------------------------
+// Errors
+// ---------------------------------------------------------------------------
+static thread_local std::string g_err;
+
+static int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+#define CK(call)                                                                                   \
+  do {                                                                                             \
+    cudaError_t _e = (call);                                                                       \
+    if (_e != cudaSuccess)                                                                         \
+      return fail(LBRR_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(_e));              \
+  } while (0)
+#define CKFFT(call)                                                                                \
+  do {                                                                                             \
+    cufftResult _r = (call);                                                                       \
+    if (_r != CUFFT_SUCCESS) return fail(LBRR_ERR_CUDA, std::string(#call) + ": cufft error " + std::to_string(_r)); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// fp16 packing contract (src/fp16.rs:4-37): RNE, NaN -> sign | 0x7c01.
+// ---------------------------------------------------------------------------
+static uint16_t f32_to_f16_bits(float x) {
+  uint32_t b;
+  std::memcpy(&b, &x, 4);
+  const uint16_t sign = static_cast<uint16_t>((b >> 16) & 0x8000u);
+  const int exp = static_cast<int>((b >> 23) & 0xFFu);
+  const uint32_t mant = b & 0x7FFFFFu;
+  if (exp == 0xFF) return static_cast<uint16_t>(sign | 0x7C00u | (mant != 0 ? 1u : 0u));
+  const int e = exp - 127 + 15;
+  if (e >= 0x1F) return static_cast<uint16_t>(sign | 0x7C00u);
+  if (e <= 0) {
+    if (e < -10) return sign;
+    const uint32_t m = mant | 0x800000u;
+    const uint32_t shift = static_cast<uint32_t>(14 - e);
+    const uint32_t half = m >> shift;
+    const uint32_t rem = m & ((1u << shift) - 1u);
+    const uint32_t halfway = 1u << (shift - 1);
+    uint32_t hm = half;
+    if (rem > halfway || (rem == halfway && (half & 1u))) hm += 1;
+    return static_cast<uint16_t>(sign | hm);
+  }
+  uint32_t hm = (static_cast<uint32_t>(e) << 10) | (mant >> 13);
+  const uint32_t rem = mant & 0x1FFFu;
+  if (rem > 0x1000u || (rem == 0x1000u && (hm & 1u))) hm += 1;
+  return static_cast<uint16_t>(sign | hm);
+}
+static float f16_bits_to_f32(uint16_t h) {
+  const uint32_t sign = (h & 0x8000u) << 16;
+  const uint32_t exp = (h >> 10) & 0x1Fu;
+  uint32_t mant = h & 0x3FFu;
+  uint32_t bits;
+  if (exp == 0) {
+    if (mant == 0) {
+      bits = sign;
+    } else {
+      int e = -1;
+      do {
+        mant <<= 1;
+        ++e;
+      } while (!(mant & 0x400u));
+      bits = sign | (static_cast<uint32_t>(127 - 15 - e) << 23) | ((mant & 0x3FFu) << 13);
+    }
+  } else if (exp == 0x1F) {
+    bits = sign | 0x7F800000u | (mant << 13);
+  } else {
+    bits = sign | ((exp - 15 + 127) << 23) | (mant << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+extern "C" uint16_t lbrr_f32_to_f16_bits(float x) { return f32_to_f16_bits(x); }
+
+// ---------------------------------------------------------------------------
+// Model geometry
+// ---------------------------------------------------------------------------
+static const int kFreqs[kNumBands] = {2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,  2,
+                                      2,  2,  2,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  4,  12, 12, 12, 12, 12, 12,
+                                      12, 12, 24, 24, 24, 24, 24, 24, 24, 24, 48, 48, 48, 48, 48, 48, 48, 48, 128, 129};
+
+struct BandGeom {
+  int d[kNumBands], f0[kNumBands], offs[kNumBands + 1];
+  int koff[kNumBands], kpad[kNumBands];  // xn / band-W column slots (multiples of 64)
+  int n2pad[kNumBands], o2[kNumBands];   // permuted W2 rows per band (multiple of 16)
+  int xn_cols, kpad_max, n2tot;
+  BandGeom() {
+    offs[0] = 0;
+    int f = 0, ko = 0, o = 0;
+    kpad_max = 0;
+    for (int b = 0; b < kNumBands; ++b) {
+      d[b] = 4 * kFreqs[b];
+      f0[b] = f;
+      f += kFreqs[b];
+      offs[b + 1] = offs[b] + d[b];
+      kpad[b] = (d[b] + 63) / 64 * 64;
+      koff[b] = ko;
+      ko += kpad[b];
+      kpad_max = std::max(kpad_max, kpad[b]);
+      n2pad[b] = (2 * d[b] + 15) / 16 * 16;
+      o2[b] = o;
+      o += n2pad[b];
+    }
+    xn_cols = ko;
+    n2tot = o;
+  }
+};
+static const BandGeom& geom() {
+  static BandGeom g;
+  return g;
+}
+
+// ---------------------------------------------------------------------------
+// Engine
+// ---------------------------------------------------------------------------
+struct StepWeights {
+  __half *wqkv, *wo, *w1, *w2;
+  float *norm_g, *gate_w, *gate_b, *ff_g, *b1, *b2;
+};
+
+struct lbrr_engine {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int64_t max_len = 0;
+  int max_T = 0;
+  bool weights_loaded = false;
+  // weights
+  void* warena = nullptr;
+  size_t warena_bytes = 0;
+  StepWeights steps[2 * kDepth];
+  float *qkv_bias16 = nullptr, *out_bias = nullptr, *final_g = nullptr;
+  __half* band_w = nullptr;
+  float *band_b = nullptr, *band_g = nullptr;
+  __half *mask_w1 = nullptr, *mask_w2 = nullptr;
+  float *mask_b1 = nullptr, *mask_b2 = nullptr;
+  int* band_tab = nullptr;  // [nb][8]: d, f0, koff, kpad, goff, o2, n2pad, 0
+  int *band_f0 = nullptr, *band_d = nullptr, *band_o2 = nullptr;
+  // per-length state
+  int64_t cur_len = -1;
+  int cur_T = -1;
+  float *cos_t = nullptr, *sin_t = nullptr, *cos_f = nullptr, *sin_f = nullptr;
+  TileDesc *tiles_band = nullptr, *tiles_m1 = nullptr, *tiles_m2 = nullptr;
+  int n_band = 0, n_m1 = 0, n_m2 = 0;
+  float* inv_env = nullptr;
+  cufftHandle plan_r2c = 0, plan_c2r = 0;
+  bool plans = false;
+  // scratch
+  void* sarena = nullptr;
+  size_t sarena_bytes = 0;
+  float *window = nullptr, *frames = nullptr, *x = nullptr, *gates = nullptr, *attn_out = nullptr, *pcm = nullptr;
+  float2 *spec = nullptr, *c2r = nullptr;
+  __half *xn = nullptr, *h16 = nullptr, *qkv = nullptr, *scaled = nullptr, *ff1 = nullptr, *xb16 = nullptr,
+         *hidden = nullptr;
+  int* status = nullptr;
+  // host staging for the end-to-end entry point
+  float* pin_in = nullptr;
+  float* pin_out = nullptr;
+  float* dev_in = nullptr;
+  float* dev_out = nullptr;
+};
+
+namespace {
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+struct Carver {
+  size_t off = 0;
+  template <class T>
+  size_t take(size_t count) {
+    off = align_up(off, 1024);
+    const size_t o = off;
+    off += count * sizeof(T);
+    return o;
+  }
+};
+}  // namespace
+
+extern "C" const char* lbrr_last_error(void) { return g_err.c_str(); }
+// Lets the host-only translation units (safetensors.cpp) report errors through
+// the same thread-local message.
+extern "C" int lbrr_set_error_for_host(int code, const char* msg) { return fail(code, msg ? msg : ""); }
+extern "C" int lbrr_abi_version(void) { return 1; }
+
+extern "C" int lbrr_default_model(lbrr_model_desc* d, int32_t* freqs_out, int32_t capacity) {
+  if (!d || !freqs_out || capacity < kNumBands) return fail(LBRR_ERR_INVALID, "lbrr_default_model: need 62 slots");
+  for (int b = 0; b < kNumBands; ++b) freqs_out[b] = kFreqs[b];
+  d->dim = kDim;
+  d->depth = kDepth;
+  d->heads = kHeads;
+  d->dim_head = kDimHead;
+  d->num_stems = kStems;
+  d->mlp_expansion = 4;
+  d->n_fft = kNfft;
+  d->hop = kHop;
+  d->sample_rate = 44100;
+  d->num_bands = kNumBands;
+  d->freqs_per_band = freqs_out;
+  return LBRR_OK;
+}
+
+static int check_desc(const lbrr_model_desc* d) {
+  if (!d) return LBRR_OK;  // NULL = the default model
+  if (d->dim != kDim || d->depth != kDepth || d->heads != kHeads || d->dim_head != kDimHead ||
+      d->num_stems != kStems || d->mlp_expansion != 4 || d->n_fft != kNfft || d->hop != kHop ||
+      d->num_bands != kNumBands || !d->freqs_per_band)
+    return fail(LBRR_ERR_INVALID, "unsupported model configuration (only the 62-band, 12-layer, dim-256 "
+                                  "BS-RoFormer of logic_bs_roformer.yaml is built)");
+  int sum = 0;
+  for (int b = 0; b < kNumBands; ++b) {
+    if (d->freqs_per_band[b] != kFreqs[b]) return fail(LBRR_ERR_INVALID, "unsupported freqs_per_band");
+    sum += d->freqs_per_band[b];
+  }
+  if (sum != kBins) return fail(LBRR_ERR_INVALID, "freqs_per_band must sum to 1025");
+  return LBRR_OK;
+}
+
+static int T_of(int64_t len) { return static_cast<int>(len / kHop + 1); }
+
+extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64_t max_len, lbrr_engine** out) {
+  if (!out) return fail(LBRR_ERR_INVALID, "out is NULL");
+  *out = nullptr;
+  if (int rc = check_desc(desc)) return rc;
+  if (max_len <= kNfft / 2 || max_len > (1ll << 26))
+    return fail(LBRR_ERR_INVALID, "max_chunk_samples must be in (1024, 2^26]");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(LBRR_ERR_INVALID, "device index out of range");
+  DeviceGuard g(device);
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, device));
+  if (prop.major != 10) return fail(LBRR_ERR_INVALID, "this build targets sm_100a (B200); found sm_" +
+                                                        std::to_string(prop.major) + std::to_string(prop.minor));
+  lbrr_engine* e = new lbrr_engine();
+  e->device = device;
+  e->max_len = max_len;
+  e->max_T = T_of(max_len);
+  const BandGeom& G = geom();
+  const size_t T = e->max_T, M = T * kNumBands;
+  // ---- weights arena ----
+  Carver w;
+  size_t o_steps[2 * kDepth][10];
+  for (int s = 0; s < 2 * kDepth; ++s) {
+    o_steps[s][0] = w.take<__half>(1536 * 256);
+    o_steps[s][1] = w.take<__half>(256 * 512);
+    o_steps[s][2] = w.take<__half>(1024 * 256);
+    o_steps[s][3] = w.take<__half>(256 * 1024);
+    o_steps[s][4] = w.take<float>(256);
+    o_steps[s][5] = w.take<float>(8 * 256);
+    o_steps[s][6] = w.take<float>(8);
+    o_steps[s][7] = w.take<float>(256);
+    o_steps[s][8] = w.take<float>(1024);
+    o_steps[s][9] = w.take<float>(256);
+  }
+  const size_t o_qb = w.take<float>(1536), o_ob = w.take<float>(256), o_fg = w.take<float>(256);
+  const size_t o_bw = w.take<__half>(static_cast<size_t>(kNumBands) * 256 * G.kpad_max);
+  const size_t o_bb = w.take<float>(kNumBands * 256), o_bg = w.take<float>(G.offs[kNumBands]);
+  const size_t o_m1 = w.take<__half>(static_cast<size_t>(kStems) * kNumBands * 1024 * 256);
+  const size_t o_mb1 = w.take<float>(static_cast<size_t>(kStems) * kNumBands * 1024);
+  const size_t o_m2 = w.take<__half>(static_cast<size_t>(kStems) * G.n2tot * 1024);
+  const size_t o_mb2 = w.take<float>(static_cast<size_t>(kStems) * G.n2tot);
+  e->warena_bytes = align_up(w.off, 1024);
+  // ---- scratch arena ----
+  Carver s;
+  const size_t o_win = s.take<float>(kNfft), o_fr = s.take<float>(2 * T * kNfft), o_sp = s.take<float2>(2 * T * kBins);
+  const size_t o_xn = s.take<__half>(T * G.xn_cols), o_x = s.take<float>(M * 256), o_h = s.take<__half>(M * 256);
+  const size_t o_g = s.take<float>(M * 8), o_qkv = s.take<__half>(M * 1536), o_sc = s.take<__half>(M * 512);
+  const size_t o_ao = s.take<float>(M * 256), o_ff = s.take<__half>(M * 1024), o_xb = s.take<__half>(M * 256);
+  const size_t o_hid = s.take<__half>(static_cast<size_t>(kStems) * M * 1024);
+  const size_t o_c2r = s.take<float2>(static_cast<size_t>(2 * kStems) * T * kBins);
+  const size_t o_pcm = s.take<float>(static_cast<size_t>(2 * kStems) * T * kNfft);
+  const size_t o_st = s.take<int>(64);
+  const size_t o_tab = s.take<int>(kNumBands * 8), o_f0 = s.take<int>(kNumBands), o_d = s.take<int>(kNumBands),
+               o_o2 = s.take<int>(kNumBands);
+  const size_t o_din = s.take<float>(2 * max_len), o_dout = s.take<float>(2 * kStems * max_len);
+  e->sarena_bytes = align_up(s.off, 1024);
+
+  auto cleanup = [&](int rc) {
+    lbrr_engine_destroy(e);
+    return rc;
+  };
+  cudaError_t ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+  if (ce == cudaSuccess) ce = cudaMalloc(&e->warena, e->warena_bytes);
+  if (ce == cudaSuccess) ce = cudaMalloc(&e->sarena, e->sarena_bytes);
+  if (ce == cudaSuccess) ce = cudaMemset(e->warena, 0, e->warena_bytes);
+  if (ce == cudaSuccess) ce = cudaMemset(e->sarena, 0, e->sarena_bytes);
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->pin_in, 2 * max_len * sizeof(float));
+  if (ce == cudaSuccess) ce = cudaMallocHost(&e->pin_out, 2 * kStems * max_len * sizeof(float));
+  if (ce != cudaSuccess) return cleanup(fail(LBRR_ERR_CUDA, std::string("engine allocation: ") + cudaGetErrorString(ce)));
+  char* W = static_cast<char*>(e->warena);
+  char* S = static_cast<char*>(e->sarena);
+  for (int k = 0; k < 2 * kDepth; ++k) {
+    StepWeights& sw = e->steps[k];
+    sw.wqkv = reinterpret_cast<__half*>(W + o_steps[k][0]);
+    sw.wo = reinterpret_cast<__half*>(W + o_steps[k][1]);
+    sw.w1 = reinterpret_cast<__half*>(W + o_steps[k][2]);
+    sw.w2 = reinterpret_cast<__half*>(W + o_steps[k][3]);
+    sw.norm_g = reinterpret_cast<float*>(W + o_steps[k][4]);
+    sw.gate_w = reinterpret_cast<float*>(W + o_steps[k][5]);
+    sw.gate_b = reinterpret_cast<float*>(W + o_steps[k][6]);
+    sw.ff_g = reinterpret_cast<float*>(W + o_steps[k][7]);
+    sw.b1 = reinterpret_cast<float*>(W + o_steps[k][8]);
+    sw.b2 = reinterpret_cast<float*>(W + o_steps[k][9]);
+  }
+  e->qkv_bias16 = reinterpret_cast<float*>(W + o_qb);
+  e->out_bias = reinterpret_cast<float*>(W + o_ob);
+  e->final_g = reinterpret_cast<float*>(W + o_fg);
+  e->band_w = reinterpret_cast<__half*>(W + o_bw);
+  e->band_b = reinterpret_cast<float*>(W + o_bb);
+  e->band_g = reinterpret_cast<float*>(W + o_bg);
+  e->mask_w1 = reinterpret_cast<__half*>(W + o_m1);
+  e->mask_b1 = reinterpret_cast<float*>(W + o_mb1);
+  e->mask_w2 = reinterpret_cast<__half*>(W + o_m2);
+  e->mask_b2 = reinterpret_cast<float*>(W + o_mb2);
+  e->band_tab = reinterpret_cast<int*>(S + o_tab);
+  e->band_f0 = reinterpret_cast<int*>(S + o_f0);
+  e->band_d = reinterpret_cast<int*>(S + o_d);
+  e->band_o2 = reinterpret_cast<int*>(S + o_o2);
+  e->window = reinterpret_cast<float*>(S + o_win);
+  e->frames = reinterpret_cast<float*>(S + o_fr);
+  e->spec = reinterpret_cast<float2*>(S + o_sp);
+  e->xn = reinterpret_cast<__half*>(S + o_xn);
+  e->x = reinterpret_cast<float*>(S + o_x);
+  e->h16 = reinterpret_cast<__half*>(S + o_h);
+  e->gates = reinterpret_cast<float*>(S + o_g);
+  e->qkv = reinterpret_cast<__half*>(S + o_qkv);
+  e->scaled = reinterpret_cast<__half*>(S + o_sc);
+  e->attn_out = reinterpret_cast<float*>(S + o_ao);
+  e->ff1 = reinterpret_cast<__half*>(S + o_ff);
+  e->xb16 = reinterpret_cast<__half*>(S + o_xb);
+  e->hidden = reinterpret_cast<__half*>(S + o_hid);
+  e->c2r = reinterpret_cast<float2*>(S + o_c2r);
+  e->pcm = reinterpret_cast<float*>(S + o_pcm);
+  e->status = reinterpret_cast<int*>(S + o_st);
+  e->dev_in = reinterpret_cast<float*>(S + o_din);
+  e->dev_out = reinterpret_cast<float*>(S + o_dout);
+  // constant tables: periodic Hann (f64 -> f32, src/stft.rs:25-29) and band geometry
+  std::vector<float> win(kNfft);
+  for (int i = 0; i < kNfft; ++i) win[i] = static_cast<float>(0.5 * (1.0 - std::cos(2.0 * M_PI * i / kNfft)));
+  std::vector<int> tab(kNumBands * 8), f0(kNumBands), dd(kNumBands), o2(kNumBands);
+  for (int b = 0; b < kNumBands; ++b) {
+    int* r = &tab[b * 8];
+    r[0] = G.d[b];
+    r[1] = G.f0[b];
+    r[2] = G.koff[b];
+    r[3] = G.kpad[b];
+    r[4] = G.offs[b];
+    r[5] = G.o2[b];
+    r[6] = G.n2pad[b];
+    r[7] = 0;
+    f0[b] = G.f0[b];
+    dd[b] = G.d[b];
+    o2[b] = G.o2[b];
+  }
+  ce = cudaMemcpy(e->window, win.data(), win.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->band_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->band_f0, f0.data(), f0.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->band_d, dd.data(), dd.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->band_o2, o2.data(), o2.size() * 4, cudaMemcpyHostToDevice);
+  if (ce != cudaSuccess) return cleanup(fail(LBRR_ERR_CUDA, std::string("engine tables: ") + cudaGetErrorString(ce)));
+  *out = e;
+  return LBRR_OK;
+}
+
+extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
+  if (!e) return;
+  DeviceGuard g(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  if (e->plans) {
+    cufftDestroy(e->plan_r2c);
+    cufftDestroy(e->plan_c2r);
+  }
+  cudaFree(e->cos_t);
+  cudaFree(e->tiles_band);
+  cudaFree(e->inv_env);
+  cudaFree(e->warena);
+  cudaFree(e->sarena);
+  if (e->pin_in) cudaFreeHost(e->pin_in);
+  if (e->pin_out) cudaFreeHost(e->pin_out);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+extern "C" int lbrr_engine_memory(const lbrr_engine* e, int64_t* wb, int64_t* sb) {
+  if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
+  if (wb) *wb = static_cast<int64_t>(e->warena_bytes);
+  if (sb) *sb = static_cast<int64_t>(e->sarena_bytes);
+  return LBRR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Weights
+// ---------------------------------------------------------------------------
+namespace {
+struct ViewMap {
+  std::map<std::string, const lbrr_weight_view*> m;
+  std::map<std::string, int> used;
+  std::string err;
+  const float* take(const std::string& name, int64_t numel) {
+    auto it = m.find(name);
+    if (it == m.end()) {
+      if (err.empty()) err = "missing tensor " + name;
+      return nullptr;
+    }
+    if (used[name]++) {
+      if (err.empty()) err = "duplicate key use: " + name;
+      return nullptr;
+    }
+    if (it->second->numel != numel) {
+      if (err.empty())
+        err = name + ": len " + std::to_string(it->second->numel) + " != " + std::to_string(numel);
+      return nullptr;
+    }
+    if (!it->second->data) {
+      if (err.empty()) err = name + ": NULL data";
+      return nullptr;
+    }
+    return it->second->data;
+  }
+};
+void pack16(uint16_t* dst, const float* src, size_t n) {
+  for (size_t i = 0; i < n; ++i) dst[i] = f32_to_f16_bits(src[i]);
+}
+}  // namespace
+
+extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size_t n) {
+  if (!e || (!views && n)) return fail(LBRR_ERR_INVALID, "NULL engine or views");
+  DeviceGuard g(e->device);
+  const BandGeom& G = geom();
+  ViewMap vm;
+  for (size_t i = 0; i < n; ++i) {
+    if (!views[i].name) return fail(LBRR_ERR_WEIGHTS, "weight view without a name");
+    if (!vm.m.emplace(views[i].name, &views[i]).second)
+      return fail(LBRR_ERR_WEIGHTS, std::string("duplicate tensor ") + views[i].name);
+  }
+  // host image of the weight arena
+  std::vector<uint8_t> host(e->warena_bytes, 0);
+  auto hp = [&](const void* dev_ptr) { return host.data() + (static_cast<const char*>(dev_ptr) - static_cast<const char*>(e->warena)); };
+  const float* sq = vm.take("linear_62_bias_0", 1536);
+  const float* so = vm.take("linear_64_bias_0", 256);
+  if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
+  {
+    float* qb = reinterpret_cast<float*>(hp(e->qkv_bias16));
+    for (int i = 0; i < 1536; ++i) qb[i] = f16_bits_to_f32(f32_to_f16_bits(sq[i]));  // src/main.rs:5960-5962
+    std::memcpy(hp(e->out_bias), so, 256 * 4);
+  }
+  for (int l = 0; l < kDepth; ++l) {
+    for (int a = 0; a < 2; ++a) {
+      const StepWeights& sw = e->steps[l * 2 + a];
+      const std::string p = "layers." + std::to_string(l) + "." + std::to_string(a) + ".layers.0.0";
+      const std::string fp = "layers." + std::to_string(l) + "." + std::to_string(a) + ".layers.0.1.net";
+      const float* ng = vm.take(p + ".norm.gamma", 256);
+      const float* wq = vm.take(p + ".to_qkv.weight", 1536 * 256);
+      const float* wg = vm.take(p + ".to_gates.weight", 8 * 256);
+      const float* bg = vm.take(p + ".to_gates.bias", 8);
+      const float* wo = vm.take(p + ".to_out.0.weight", 256 * 512);
+      const float* g0 = vm.take(fp + ".0.gamma", 256);
+      const float* w1 = vm.take(fp + ".1.weight", 1024 * 256);
+      const float* b1 = vm.take(fp + ".1.bias", 1024);
+      const float* w2 = vm.take(fp + ".4.weight", 256 * 1024);
+      const float* b2 = vm.take(fp + ".4.bias", 256);
+      const float* qbias = vm.take(p + ".to_qkv.bias", 1536);
+      const float* obias = vm.take(p + ".to_out.0.bias", 256);
+      const float* freqs = vm.take(p + ".rotary_embed.freqs", 32);
+      if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
+      // shared biases must be byte-equal (src/weights.rs:362-372)
+      if (std::memcmp(qbias, sq, 1536 * 4)) return fail(LBRR_ERR_WEIGHTS, p + ".to_qkv.bias != linear_62_bias_0");
+      if (std::memcmp(obias, so, 256 * 4)) return fail(LBRR_ERR_WEIGHTS, p + ".to_out.0.bias != linear_64_bias_0");
+      // rotary freqs analytic (src/weights.rs:375-382)
+      for (int i = 0; i < 32; ++i) {
+        const float want = 1.0f / std::pow(10000.0f, (2.0f * i) / 64.0f);
+        if (!(std::fabs(freqs[i] - want) <= 1e-6f))
+          return fail(LBRR_ERR_WEIGHTS, "rotary freqs[" + std::to_string(i) + "] != analytic in " + p);
+      }
+      pack16(reinterpret_cast<uint16_t*>(hp(sw.wqkv)), wq, 1536 * 256);
+      pack16(reinterpret_cast<uint16_t*>(hp(sw.wo)), wo, 256 * 512);
+      pack16(reinterpret_cast<uint16_t*>(hp(sw.w1)), w1, 1024 * 256);
+      pack16(reinterpret_cast<uint16_t*>(hp(sw.w2)), w2, 256 * 1024);
+      std::memcpy(hp(sw.norm_g), ng, 256 * 4);
+      std::memcpy(hp(sw.gate_w), wg, 8 * 256 * 4);
+      std::memcpy(hp(sw.gate_b), bg, 8 * 4);
+      std::memcpy(hp(sw.ff_g), g0, 256 * 4);
+      std::memcpy(hp(sw.b1), b1, 1024 * 4);
+      std::memcpy(hp(sw.b2), b2, 256 * 4);
+    }
+  }
+  const float* fg = vm.take("final_norm.gamma", 256);
+  if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
+  std::memcpy(hp(e->final_g), fg, 256 * 4);
+  // band split: W [256][d_b] -> rows b*256+n, columns [0, d_b) of a kpad_max-wide slot
+  for (int b = 0; b < kNumBands; ++b) {
+    const std::string p = "band_split.to_features." + std::to_string(b);
+    const int d = G.d[b];
+    const float* gm = vm.take(p + ".0.gamma", d);
+    const float* wb = vm.take(p + ".1.weight", 256 * d);
+    const float* bb = vm.take(p + ".1.bias", 256);
+    if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
+    uint16_t* dst = reinterpret_cast<uint16_t*>(hp(e->band_w)) + static_cast<size_t>(b) * 256 * G.kpad_max;
+    for (int nn = 0; nn < 256; ++nn) pack16(dst + static_cast<size_t>(nn) * G.kpad_max, wb + static_cast<size_t>(nn) * d, d);
+    std::memcpy(reinterpret_cast<float*>(hp(e->band_b)) + b * 256, bb, 256 * 4);
+    std::memcpy(reinterpret_cast<float*>(hp(e->band_g)) + G.offs[b], gm, d * 4);
+  }
+  // mask estimators: W1 [1024][256] per (stem, band); W2 rows interleaved (a_d, g_d)
+  for (int s = 0; s < kStems; ++s) {
+    for (int b = 0; b < kNumBands; ++b) {
+      const std::string p = "mask_estimators." + std::to_string(s) + ".to_freqs." + std::to_string(b) + ".0";
+      const int d = G.d[b];
+      const float* w1 = vm.take(p + ".0.weight", 1024 * 256);
+      const float* b1 = vm.take(p + ".0.bias", 1024);
+      const float* w2 = vm.take(p + ".2.weight", static_cast<int64_t>(2 * d) * 1024);
+      const float* b2 = vm.take(p + ".2.bias", 2 * d);
+      if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
+      const size_t grp = static_cast<size_t>(s) * kNumBands + b;
+      pack16(reinterpret_cast<uint16_t*>(hp(e->mask_w1)) + grp * 1024 * 256, w1, 1024 * 256);
+      std::memcpy(reinterpret_cast<float*>(hp(e->mask_b1)) + grp * 1024, b1, 1024 * 4);
+      uint16_t* w2d = reinterpret_cast<uint16_t*>(hp(e->mask_w2)) + (static_cast<size_t>(s) * G.n2tot + G.o2[b]) * 1024;
+      float* b2d = reinterpret_cast<float*>(hp(e->mask_b2)) + static_cast<size_t>(s) * G.n2tot + G.o2[b];
+      for (int j = 0; j < G.n2pad[b]; ++j) {
+        const int dd = j >> 1;
+        if (dd < d) {
+          const int src = (j & 1) ? d + dd : dd;
+          pack16(w2d + static_cast<size_t>(j) * 1024, w2 + static_cast<size_t>(src) * 1024, 1024);
+          b2d[j] = b2[src];
+        }
+      }
+    }
+  }
+  // every checkpoint key consumed (src/weights.rs:428-432)
+  for (auto& kv : vm.m)
+    if (!vm.used.count(kv.first))
+      return fail(LBRR_ERR_WEIGHTS, "unconsumed key " + kv.first);
+  CK(cudaMemcpy(e->warena, host.data(), host.size(), cudaMemcpyHostToDevice));
+  e->weights_loaded = true;
+  return LBRR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Per-length setup
+// ---------------------------------------------------------------------------
+static void rope_table(int P, std::vector<float>& c, std::vector<float>& s) {
+  c.resize(static_cast<size_t>(P) * 32);
+  s.resize(static_cast<size_t>(P) * 32);
+  for (int p = 0; p < P; ++p)
+    for (int i = 0; i < 32; ++i) {
+      // angle in f64, rounded to f32, then cos/sin of that f32 (src/main.rs:7678-7681)
+      const float a = static_cast<float>(p * (1.0 / std::pow(10000.0, 2.0 * i / 64.0)));
+      c[p * 32 + i] = static_cast<float>(std::cos(static_cast<double>(a)));
+      s[p * 32 + i] = static_cast<float>(std::sin(static_cast<double>(a)));
+    }
+}
+
+static int setup_length(lbrr_engine* e, int64_t len) {
+  if (e->cur_len == len) return LBRR_OK;
+  const BandGeom& G = geom();
+  const int T = T_of(len);
+  const int mt = (T + 127) / 128;
+  // RoPE tables (time: T positions, freq: 62) -- one allocation for the tables,
+  // tile tables follow in a second allocation, both released on the next change
+  // the previous length's tables may still be read by queued work on any stream
+  CK(cudaDeviceSynchronize());
+  cudaFree(e->cos_t);
+  cudaFree(e->tiles_band);
+  cudaFree(e->inv_env);
+  e->cos_t = nullptr;
+  e->tiles_band = nullptr;
+  e->inv_env = nullptr;
+  std::vector<float> ct, st, cf, sf;
+  rope_table(T, ct, st);
+  rope_table(kNumBands, cf, sf);
+  float* tabs = nullptr;
+  CK(cudaMalloc(&tabs, (2 * ct.size() + 2 * cf.size()) * sizeof(float)));
+  e->cos_t = tabs;
+  e->sin_t = tabs + ct.size();
+  e->cos_f = tabs + 2 * ct.size();
+  e->sin_f = tabs + 2 * ct.size() + cf.size();
+  CK(cudaMemcpy(e->cos_t, ct.data(), ct.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(e->sin_t, st.data(), st.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(e->cos_f, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(e->sin_f, sf.data(), sf.size() * 4, cudaMemcpyHostToDevice));
+  // grouped GEMM tile tables
+  std::vector<TileDesc> tb, t1, t2;
+  for (int b = 0; b < kNumBands; ++b)
+    for (int m = 0; m < mt; ++m)
+      tb.push_back({m * 128, G.koff[b], b * 256, G.kpad[b] / 64, 256, m * 128, std::min(128, T - m * 128), b});
+  for (int s = 0; s < kStems; ++s)
+    for (int b = 0; b < kNumBands; ++b)
+      for (int m = 0; m < mt; ++m)
+        for (int nt = 0; nt < 4; ++nt) {
+          const int grp = s * kNumBands + b;
+          t1.push_back({b * T + m * 128, 0, grp * 1024 + nt * 256, 4, 256, m * 128, std::min(128, T - m * 128),
+                        grp * 4 + nt});
+        }
+  for (int s = 0; s < kStems; ++s)
+    for (int b = 0; b < kNumBands; ++b)
+      for (int m = 0; m < mt; ++m)
+        for (int nt = 0; nt * 256 < G.n2pad[b]; ++nt) {
+          const int grp = s * kNumBands + b;
+          t2.push_back({grp * T + m * 128, 0, s * G.n2tot + G.o2[b] + nt * 256, 16,
+                        std::min(256, G.n2pad[b] - nt * 256), m * 128, std::min(128, T - m * 128),
+                        (s << 16) | (b << 8) | nt});
+        }
+  TileDesc* tiles = nullptr;
+  CK(cudaMalloc(&tiles, (tb.size() + t1.size() + t2.size()) * sizeof(TileDesc)));
+  e->tiles_band = tiles;
+  e->tiles_m1 = tiles + tb.size();
+  e->tiles_m2 = tiles + tb.size() + t1.size();
+  e->n_band = static_cast<int>(tb.size());
+  e->n_m1 = static_cast<int>(t1.size());
+  e->n_m2 = static_cast<int>(t2.size());
+  CK(cudaMemcpy(e->tiles_band, tb.data(), tb.size() * sizeof(TileDesc), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(e->tiles_m1, t1.data(), t1.size() * sizeof(TileDesc), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(e->tiles_m2, t2.data(), t2.size() * sizeof(TileDesc), cudaMemcpyHostToDevice));
+  // ISTFT inverse window envelope over len + n_fft samples (benchmark::istft_inverse, src/benchmark.rs:129-142)
+  {
+    std::vector<float> win(kNfft), env(static_cast<size_t>(len) + kNfft, 0.f);
+    for (int i = 0; i < kNfft; ++i) win[i] = static_cast<float>(0.5 * (1.0 - std::cos(2.0 * M_PI * i / kNfft)));
+    for (int t = 0; t < T; ++t)
+      for (int nn = 0; nn < kNfft; ++nn) {
+        const size_t p = static_cast<size_t>(t) * kHop + nn;
+        if (p < env.size()) env[p] += win[nn] * win[nn];
+      }
+    for (auto& v : env) v = v > 1e-8f ? 1.0f / v : 0.f;
+    CK(cudaMalloc(&e->inv_env, env.size() * sizeof(float)));
+    CK(cudaMemcpy(e->inv_env, env.data(), env.size() * 4, cudaMemcpyHostToDevice));
+  }
+  // cuFFT plans: R2C batch 2T (src/stft.rs:36-45), C2R batch 12T
+  if (e->cur_T != T) {
+    if (e->plans) {
+      cufftDestroy(e->plan_r2c);
+      cufftDestroy(e->plan_c2r);
+      e->plans = false;
+    }
+    int n[1] = {kNfft};
+    int inr[1] = {kNfft}, outc[1] = {kBins};
+    CKFFT(cufftPlanMany(&e->plan_r2c, 1, n, inr, 1, kNfft, outc, 1, kBins, CUFFT_R2C, 2 * T));
+    CKFFT(cufftPlanMany(&e->plan_c2r, 1, n, outc, 1, kBins, inr, 1, kNfft, CUFFT_C2R, 2 * kStems * T));
+    e->plans = true;
+  }
+  e->cur_T = T;
+  e->cur_len = len;
+  return LBRR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+#define CKL(call)                                                                                  \
+  do {                                                                                             \
+    cudaError_t _e = (call);                                                                       \
+    if (_e != cudaSuccess) return fail(LBRR_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t st) {
+  const BandGeom& G = geom();
+  const int T = e->cur_T;
+  CKL(stft_frames(x, e->window, e->frames, static_cast<int>(len), T, st));
+  CKFFT(cufftSetStream(e->plan_r2c, st));
+  CKFFT(cufftExecR2C(e->plan_r2c, e->frames, reinterpret_cast<cufftComplex*>(e->spec)));
+  CKL(band_norm(e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols, T, kNumBands, st));
+  CKL(gemm_bandsplit(e->xn, G.xn_cols, e->band_w, G.kpad_max, e->band_b, e->x, T, kNumBands, e->tiles_band,
+                     e->n_band, e->status, st));
+  return LBRR_OK;
+}
+
+static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
+  const int T = e->cur_T, M = T * kNumBands, axis = k & 1;
+  const StepWeights& w = e->steps[k];
+  CKL(norm_gates(e->x, w.norm_g, w.gate_w, w.gate_b, e->h16, e->gates, M, st));
+  CKL(gemm_qkv(e->h16, w.wqkv, e->qkv_bias16, axis == 0 ? e->cos_t : e->cos_f, axis == 0 ? e->sin_t : e->sin_f,
+               e->qkv, M, kNumBands, axis, e->status, st));
+  CKL(attention_fwd(e->qkv, e->gates, e->scaled, T, kNumBands, axis, e->status, st));
+  CKL(gemm_outproj_norm(e->scaled, w.wo, e->out_bias, e->x, w.ff_g, e->attn_out, e->h16, M, e->status, st));
+  CKL(gemm_ff1_gelu(e->h16, w.w1, w.b1, e->ff1, M, e->status, st));
+  CKL(gemm_ff2_resid(e->ff1, w.w2, w.b2, e->attn_out, e->x, M, e->status, st));
+  return LBRR_OK;
+}
+
+static int run_back(lbrr_engine* e, int64_t len, float* out, cudaStream_t st) {
+  const BandGeom& G = geom();
+  const int T = e->cur_T;
+  CKL(final_norm_bandmajor(e->x, e->final_g, e->xb16, T, kNumBands, st));
+  CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, T, kStems * kNumBands, e->tiles_m1, e->n_m1, e->status,
+                 st));
+  CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
+                 G.n2tot, e->tiles_m2, e->n_m2, e->status, st));
+  CKFFT(cufftSetStream(e->plan_c2r, st));
+  CKFFT(cufftExecC2R(e->plan_c2r, reinterpret_cast<cufftComplex*>(e->c2r), e->pcm));
+  CKL(istft_ola(e->pcm, e->window, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
+  return LBRR_OK;
+}
+
+static int check_forward_args(lbrr_engine* e, const void* x, int64_t len, const void* out) {
+  if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
+  if (!x || !out) return fail(LBRR_ERR_INVALID, "NULL buffer");
+  if (!e->weights_loaded) return fail(LBRR_ERR_STATE, "weights not loaded");
+  if (len <= kNfft / 2) return fail(LBRR_ERR_INVALID, "single-block input needs len > n_fft/2 (1024)");
+  if (len > e->max_len) return fail(LBRR_ERR_INVALID, "len exceeds the engine's max_chunk_samples");
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_forward_chunk(lbrr_engine* e, const float* x, int64_t len, float* out, void* stream) {
+  if (int rc = check_forward_args(e, x, len, out)) return rc;
+  DeviceGuard g(e->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+  if (int rc = setup_length(e, len)) return rc;
+  if (int rc = run_front(e, x, len, st)) return rc;
+  for (int k = 0; k < 2 * kDepth; ++k)
+    if (int rc = run_step(e, k, st)) return rc;
+  return run_back(e, len, out, st);
+}
+
+extern "C" int lbrr_forward_trunk(lbrr_engine* e, const float* x, int64_t len, int n_steps, float* x_out,
+                                  void* stream) {
+  if (int rc = check_forward_args(e, x, len, x_out)) return rc;
+  if (n_steps < 0 || n_steps > 2 * kDepth) return fail(LBRR_ERR_INVALID, "n_steps must be in [0, 24]");
+  DeviceGuard g(e->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+  if (int rc = setup_length(e, len)) return rc;
+  if (int rc = run_front(e, x, len, st)) return rc;
+  for (int k = 0; k < n_steps; ++k)
+    if (int rc = run_step(e, k, st)) return rc;
+  CK(cudaMemcpyAsync(x_out, e->x, static_cast<size_t>(e->cur_T) * kNumBands * 256 * 4, cudaMemcpyDeviceToDevice, st));
+  return LBRR_OK;
+}
+
+static int check_status(int* status_dev, cudaStream_t st) {
+  int h = 0;
+  CK(cudaMemcpyAsync(&h, status_dev, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (h != 0) {
+    cudaMemsetAsync(status_dev, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    return fail(LBRR_ERR_DEVICE, "kernel status " + std::to_string(h) +
+                                     (h == kDevWaitTimeout ? " (pipeline wait timed out)" : "") +
+                                     (h == kDevSmemMisaligned ? " (shared memory misaligned)" : ""));
+  }
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_engine_sync(lbrr_engine* e) {
+  if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
+  DeviceGuard g(e->device);
+  CK(cudaStreamSynchronize(e->stream));
+  return check_status(e->status, e->stream);
+}
+
+extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t len, float* outh) {
+  if (int rc = check_forward_args(e, xh, len, outh)) return rc;
+  DeviceGuard g(e->device);
+  const size_t in_b = static_cast<size_t>(len) * 2 * sizeof(float);
+  const size_t out_b = static_cast<size_t>(len) * 2 * kStems * sizeof(float);
+  std::memcpy(e->pin_in, xh, in_b);
+  CK(cudaMemcpyAsync(e->dev_in, e->pin_in, in_b, cudaMemcpyHostToDevice, e->stream));
+  if (int rc = lbrr_forward_chunk(e, e->dev_in, len, e->dev_out, e->stream)) return rc;
+  CK(cudaMemcpyAsync(e->pin_out, e->dev_out, out_b, cudaMemcpyDeviceToHost, e->stream));
+  if (int rc = check_status(e->status, e->stream)) return rc;
+  std::memcpy(outh, e->pin_out, out_b);
+  return LBRR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Whole song
+// ---------------------------------------------------------------------------
+__global__ void ola_accumulate_kernel(const float* __restrict__ y, float* __restrict__ result,
+                                      float* __restrict__ counter, long long out_len, long long s, int take, int c,
+                                      int border, int is_first, int is_last, int chunk_stride, int channels) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= take) return;
+  float wf = 1.0f;
+  if (j < border) wf = static_cast<float>(j) / static_cast<float>(border);
+  const int j2 = c - 1 - j;
+  if (j2 < border) wf = static_cast<float>(j2) / static_cast<float>(border);
+  if (is_first && j < border) wf = 1.0f;
+  if (is_last && j + border >= c) wf = 1.0f;
+  counter[s + j] += wf * wf;
+  for (int sc = 0; sc < channels; ++sc) result[sc * out_len + s + j] += y[static_cast<long long>(sc) * chunk_stride + j] * wf;
+}
+
+__global__ void ola_finalize_kernel(const float* __restrict__ result, const float* __restrict__ counter,
+                                    float* __restrict__ out, long long out_len, long long border, long long len,
+                                    int channels) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= channels * len) return;
+  const long long sc = i / len, k = i % len;
+  const float c = counter[border + k];
+  out[i] = result[sc * out_len + border + k] / fmaxf(c, 1e-8f);
+}
+
+namespace {
+std::vector<int64_t> chunk_starts(int64_t len, int64_t chunk, int64_t step, int64_t border) {
+  std::vector<int64_t> v;
+  const int64_t needed = border + len;
+  const int64_t last = std::max<int64_t>(0, (needed - chunk + step - 1) / step);
+  for (int64_t i = 0; i <= last; ++i) v.push_back(i * step);
+  return v;
+}
+}  // namespace
+
+extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const float* xh, int64_t len,
+                                  const lbrr_chunk_plan* plan, float* outh) {
+  if (!engines || n <= 0 || !xh || !outh) return fail(LBRR_ERR_INVALID, "NULL argument");
+  if (len <= 0) return fail(LBRR_ERR_INVALID, "empty audio is unsupported");
+  const lbrr_chunk_plan P = plan ? *plan : lbrr_chunk_plan{588800, 559360, 29440};
+  if (P.chunk <= kNfft / 2 || P.step <= 0 || P.step > P.chunk || P.border < 0 || 2 * P.border > P.chunk)
+    return fail(LBRR_ERR_INVALID, "invalid chunk plan");
+  for (int i = 0; i < n; ++i) {
+    if (!engines[i]) return fail(LBRR_ERR_INVALID, "NULL engine");
+    if (!engines[i]->weights_loaded) return fail(LBRR_ERR_STATE, "weights not loaded");
+    if (engines[i]->max_len < P.chunk) return fail(LBRR_ERR_INVALID, "engine scratch smaller than the chunk");
+  }
+  const auto starts = chunk_starts(len, P.chunk, P.step, P.border);
+  const int64_t needed = P.border + len;
+  const int64_t right = starts.back() + P.chunk - needed;
+  const int64_t C = P.chunk;
+  // reflect pad (tools/bench_ref.py:39-45), interleaved
+  std::vector<float> xp(static_cast<size_t>(P.border + len + right) * 2);
+  for (int64_t i = 0; i < P.border + len + right; ++i) {
+    int64_t src;
+    if (len == 1) {
+      src = 0;
+    } else {
+      const int64_t period = 2 * (len - 1);
+      int64_t p = (i - P.border) % period;
+      if (p < 0) p += period;
+      src = p < len ? p : period - p;
+    }
+    xp[2 * i] = xh[2 * src];
+    xp[2 * i + 1] = xh[2 * src + 1];
+  }
+  lbrr_engine* e0 = engines[0];
+  const int channels = 2 * kStems;
+  const size_t ybytes = static_cast<size_t>(channels) * C * sizeof(float);
+  float *result = nullptr, *counter = nullptr, *stage = nullptr, *fin = nullptr;
+  std::vector<cudaEvent_t> ev_done(n, nullptr), ev_used(n, nullptr);
+  int rc = LBRR_OK;
+  {
+    DeviceGuard g(e0->device);
+    CK(cudaMalloc(&result, static_cast<size_t>(channels) * needed * sizeof(float)));
+    CK(cudaMalloc(&counter, static_cast<size_t>(needed) * sizeof(float)));
+    CK(cudaMalloc(&stage, ybytes));
+    CK(cudaMalloc(&fin, static_cast<size_t>(channels) * len * sizeof(float)));
+    CK(cudaMemsetAsync(result, 0, static_cast<size_t>(channels) * needed * sizeof(float), e0->stream));
+    CK(cudaMemsetAsync(counter, 0, static_cast<size_t>(needed) * sizeof(float), e0->stream));
+  }
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(engines[i]->device);
+    cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming);
+    cudaEventCreateWithFlags(&ev_used[i], cudaEventDisableTiming);
+    if (i > 0 && engines[i]->device != e0->device) {
+      // direct NVLink copies when peer access exists; otherwise cudaMemcpyPeerAsync
+      // stages through host memory on its own
+      int can = 0;
+      cudaDeviceCanAccessPeer(&can, e0->device, engines[i]->device);
+      if (can) {
+        DeviceGuard g0(e0->device);
+        const cudaError_t pe = cudaDeviceEnablePeerAccess(engines[i]->device, 0);
+        if (pe != cudaSuccess && pe != cudaErrorPeerAccessAlreadyEnabled)
+          rc = fail(LBRR_ERR_PEER, std::string("enable peer access: ") + cudaGetErrorString(pe));
+        cudaGetLastError();
+      }
+    }
+  }
+  for (size_t ci = 0; rc == LBRR_OK && ci < starts.size(); ++ci) {
+    lbrr_engine* e = engines[ci % n];
+    const int slot = static_cast<int>(ci % n);
+    const int64_t s = starts[ci];
+    {
+      DeviceGuard g(e->device);
+      // the input staging slot and dev_out of this engine are free once the
+      // previous chunk's waveform was consumed by the stitching stream
+      cudaStreamWaitEvent(e->stream, ev_used[slot], 0);
+      if (cudaStreamSynchronize(e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "stream sync"); break; }
+      std::memcpy(e->pin_in, xp.data() + 2 * s, static_cast<size_t>(C) * 2 * sizeof(float));
+      if (cudaMemcpyAsync(e->dev_in, e->pin_in, static_cast<size_t>(C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
+                          e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "H2D chunk"); break; }
+      if ((rc = lbrr_forward_chunk(e, e->dev_in, C, e->dev_out, e->stream)) != LBRR_OK) break;
+      cudaEventRecord(ev_done[slot], e->stream);
+    }
+    {
+      DeviceGuard g(e0->device);
+      cudaStreamWaitEvent(e0->stream, ev_done[slot], 0);
+      const float* y = e->dev_out;
+      if (e != e0) {
+        if (cudaMemcpyPeerAsync(stage, e0->device, e->dev_out, e->device, ybytes, e0->stream) != cudaSuccess) {
+          rc = fail(LBRR_ERR_PEER, "peer copy of a chunk waveform failed");
+          break;
+        }
+        y = stage;
+      }
+      const int take = static_cast<int>(std::min<int64_t>(C, needed - s));
+      ola_accumulate_kernel<<<(take + 255) / 256, 256, 0, e0->stream>>>(
+          y, result, counter, needed, s, take, static_cast<int>(C), static_cast<int>(P.border), ci == 0,
+          ci + 1 == starts.size(), static_cast<int>(C), channels);
+      cudaEventRecord(ev_used[slot], e0->stream);
+      if (cudaGetLastError() != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "ola accumulate launch"); break; }
+    }
+  }
+  if (rc == LBRR_OK) {
+    DeviceGuard g(e0->device);
+    const long long total = static_cast<long long>(channels) * len;
+    ola_finalize_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, e0->stream>>>(
+        result, counter, fin, needed, P.border, len, channels);
+    std::vector<float> cnt(static_cast<size_t>(len));
+    cudaMemcpyAsync(cnt.data(), counter + P.border, static_cast<size_t>(len) * 4, cudaMemcpyDeviceToHost, e0->stream);
+    cudaMemcpyAsync(outh, fin, static_cast<size_t>(total) * 4, cudaMemcpyDeviceToHost, e0->stream);
+    for (int i = 0; i < n && rc == LBRR_OK; ++i) {
+      DeviceGuard g2(engines[i]->device);
+      rc = check_status(engines[i]->status, engines[i]->stream);
+    }
+    if (rc == LBRR_OK) {
+      if (cudaStreamSynchronize(e0->stream) != cudaSuccess) rc = fail(LBRR_ERR_CUDA, "final sync");
+      // demix counter must cover every output sample (src/main.rs:7776)
+      for (int64_t i = 0; rc == LBRR_OK && i < len; ++i)
+        if (!(cnt[i] > 1e-8f)) rc = fail(LBRR_ERR_STATE, "demix has uncovered output samples");
+    }
+  }
+  for (int i = 0; i < n; ++i) {
+    DeviceGuard g(engines[i]->device);
+    cudaStreamSynchronize(engines[i]->stream);
+    if (ev_done[i]) cudaEventDestroy(ev_done[i]);
+    if (ev_used[i]) cudaEventDestroy(ev_used[i]);
+  }
+  {
+    DeviceGuard g(e0->device);
+    cudaFree(result);
+    cudaFree(counter);
+    cudaFree(stage);
+    cudaFree(fin);
+  }
+  return rc;
+}
+
+// ---------------------------------------------------------------------------
+// Per-op entry points
+// ---------------------------------------------------------------------------
+static int* op_status() {
+  static std::mutex mu;
+  static std::map<int, int*> per_dev;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = per_dev.find(dev);
+  if (it != per_dev.end()) return it->second;
+  int* p = nullptr;
+  if (cudaMalloc(&p, 64 * sizeof(int)) != cudaSuccess) return nullptr;
+  cudaMemset(p, 0, 64 * sizeof(int));
+  cudaDeviceSynchronize();
+  per_dev[dev] = p;
+  return p;
+}
+
+#define OP_PROLOGUE                                                                                \
+  int* status = op_status();                                                                       \
+  if (!status) return fail(LBRR_ERR_CUDA, "op status allocation failed");                          \
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+extern "C" int lbrr_op_norm_gates(const float* x, const float* gamma, const float* gw, const float* gb, uint16_t* h16,
+                                  float* gates, int64_t rows, void* stream) {
+  if (!x || !gamma || !gw || !gb || !h16 || !gates || rows <= 0 || rows > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_norm_gates: bad arguments");
+  OP_PROLOGUE
+  (void)status;
+  CK(norm_gates(x, gamma, gw, gb, reinterpret_cast<__half*>(h16), gates, static_cast<int>(rows), st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_qkv_rope(const uint16_t* h16, const uint16_t* w16, const float* bias16, const float* cos_tab,
+                                const float* sin_tab, uint16_t* qkv, int64_t frames, int32_t bands, int32_t axis,
+                                void* stream) {
+  if (!h16 || !w16 || !bias16 || !cos_tab || !sin_tab || !qkv || frames <= 0 || bands <= 0 || (axis != 0 && axis != 1) ||
+      frames * bands > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_qkv_rope: bad arguments");
+  OP_PROLOGUE
+  CK(gemm_qkv(reinterpret_cast<const __half*>(h16), reinterpret_cast<const __half*>(w16), bias16, cos_tab, sin_tab,
+              reinterpret_cast<__half*>(qkv), static_cast<int>(frames * bands), bands, axis, status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_attention(const uint16_t* qkv, const float* gates, uint16_t* out, int64_t frames, int32_t bands,
+                                 int32_t axis, void* stream) {
+  if (!qkv || !gates || !out || frames <= 0 || bands <= 0 || (axis != 0 && axis != 1) || (axis == 1 && bands > 64) ||
+      frames * bands > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_attention: bad arguments (freq axis needs bands <= 64)");
+  OP_PROLOGUE
+  CK(attention_fwd(reinterpret_cast<const __half*>(qkv), gates, reinterpret_cast<__half*>(out),
+                   static_cast<int>(frames), bands, axis, status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_outproj_norm(const uint16_t* scaled16, const uint16_t* w16, const float* bias,
+                                    const float* resid, const float* gamma, float* attn_out, uint16_t* h16,
+                                    int64_t rows, void* stream) {
+  if (!scaled16 || !w16 || !bias || !resid || !gamma || !attn_out || !h16 || rows <= 0 || rows > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_outproj_norm: bad arguments");
+  OP_PROLOGUE
+  CK(gemm_outproj_norm(reinterpret_cast<const __half*>(scaled16), reinterpret_cast<const __half*>(w16), bias, resid,
+                       gamma, attn_out, reinterpret_cast<__half*>(h16), static_cast<int>(rows), status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_ff1_gelu(const uint16_t* h16, const uint16_t* w16, const float* b1, uint16_t* ff1,
+                                int64_t rows, void* stream) {
+  if (!h16 || !w16 || !b1 || !ff1 || rows <= 0 || rows > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_ff1_gelu: bad arguments");
+  OP_PROLOGUE
+  CK(gemm_ff1_gelu(reinterpret_cast<const __half*>(h16), reinterpret_cast<const __half*>(w16), b1,
+                   reinterpret_cast<__half*>(ff1), static_cast<int>(rows), status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const float* b2, const float* resid,
+                                 float* x, int64_t rows, void* stream) {
+  if (!ff1 || !w16 || !b2 || !resid || !x || rows <= 0 || rows > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_ff2_resid: bad arguments");
+  OP_PROLOGUE
+  CK(gemm_ff2_resid(reinterpret_cast<const __half*>(ff1), reinterpret_cast<const __half*>(w16), b2, resid, x,
+                    static_cast<int>(rows), status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_sync(void* stream) {
+  int* status = op_status();
+  if (!status) return fail(LBRR_ERR_CUDA, "op status allocation failed");
+  return check_status(status, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,67 @@
+// Internal launcher interface between the CUDA kernels and the engine / C ABI.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lbrr {
+
+constexpr int kNumBands = 62;
+constexpr int kDim = 256;
+constexpr int kHeads = 8;
+constexpr int kDimHead = 64;
+constexpr int kFF = 1024;
+constexpr int kStems = 6;
+constexpr int kNfft = 2048;
+constexpr int kHop = 512;
+constexpr int kBins = 1025;
+constexpr int kDepth = 12;
+
+// One GEMM CTA tile (A rows [a_row, a_row+128), A columns from a_col, B rows
+// [b_row, b_row+n), kblocks K-blocks of 64, epilogue rows row0.. with `rows`
+// valid, `aux` epilogue-specific).
+struct TileDesc {
+  int a_row, a_col, b_row, kblocks;
+  int n, row0, rows, aux;
+};
+
+// TMA tensor maps (fp16, 128-byte swizzle, zero OOB fill).
+cudaError_t make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                        uint32_t box_inner, uint32_t box_outer);
+cudaError_t make_map_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
+                        uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2);
+
+// ---- GEMMs (gemm.cu) -------------------------------------------------------
+cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, const float* cos, const float* sin,
+                     __half* qkv, int M, int nb, int axis, int* status, cudaStream_t st);
+cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const float* bias, const float* resid,
+                              const float* gamma, float* out, __half* h16, int M, int* status, cudaStream_t st);
+cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, __half* ff1, int M, int* status,
+                          cudaStream_t st);
+cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2, const float* resid, float* x, int M,
+                           int* status, cudaStream_t st);
+cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, int wband_cols, const float* bias,
+                           float* x, int T, int nb, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
+cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __half* hidden, int T, int groups,
+                       const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
+cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, const int* band_f0,
+                       const int* band_d, const int* band_o2, const float2* spec, float2* c2r, int T, int stems,
+                       int n2tot, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
+
+// ---- attention (attention.cu) ----------------------------------------------
+cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
+                          cudaStream_t st);
+
+// ---- bandwidth kernels (spectral.cu) ---------------------------------------
+cudaError_t stft_frames(const float* x_interleaved, const float* window, float* frames, int len, int T,
+                        cudaStream_t st);
+cudaError_t band_norm(const float2* spec, const float* gamma, const int* band_tab, __half* xn, int xn_cols, int T,
+                      int nb, cudaStream_t st);
+cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, const float* gate_b, __half* h16,
+                       float* gates, int rows, cudaStream_t st);
+cudaError_t final_norm_bandmajor(const float* x, const float* gamma, __half* xb16, int T, int nb, cudaStream_t st);
+cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_env, float* out, int len, int T,
+                      int channels, cudaStream_t st);
+
+}  // namespace lbrr

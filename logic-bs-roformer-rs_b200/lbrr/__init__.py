@@ -1,0 +1,248 @@
+"""Python binding of the B200 BS-RoFormer engine (ctypes over include/lbrr_gpu.h).
+
+The names follow the reference's GPU pipeline in ``src/main.rs``:
+``upload_weights`` (:6045-6077), ``bench_forward`` (:7014-7162, plus the
+istft_ola of :7303-7306), ``separate`` (:7598-7819) and the per-op pieces of
+``transformer_step`` (:6131-6268).  Device buffers are passed as torch CUDA
+tensors (PyTorch is only the allocator and stream provider here); every
+computation runs in ``liblbrr_b200.so``.  There is no fallback: if the library
+is missing or a call fails, a ``LbrrError`` is raised.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from pathlib import Path
+
+import numpy as np
+
+LIB_PATH = Path(__file__).resolve().parent / "liblbrr_b200.so"
+
+OK = 0
+ERR_INVALID = -1
+ERR_CUDA = -2
+ERR_WEIGHTS = -3
+ERR_DEVICE = -4
+ERR_STATE = -5
+ERR_PEER = -6
+
+CHUNK, STEP, BORDER = 588800, 559360, 29440
+STEMS = 6
+INSTRUMENTS = ["bass", "drums", "other", "vocals", "guitar", "piano"]
+
+
+class LbrrError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"lbrr error {code}: {msg}")
+        self.code = code
+
+
+class ModelDesc(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in ("dim", "depth", "heads", "dim_head", "num_stems", "mlp_expansion",
+                                         "n_fft", "hop", "sample_rate", "num_bands")] + \
+               [("freqs_per_band", C.POINTER(C.c_int32))]
+
+
+class WeightView(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("data", C.POINTER(C.c_float)), ("numel", C.c_int64)]
+
+
+class ChunkPlan(C.Structure):
+    _fields_ = [("chunk", C.c_int64), ("step", C.c_int64), ("border", C.c_int64)]
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load liblbrr_b200.so (built by logic-bs-roformer-rs_b200/build.py)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise LbrrError(ERR_STATE, f"{LIB_PATH} is missing: run logic-bs-roformer-rs_b200/build.py")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i64, i32 = C.c_void_p, C.c_int64, C.c_int32
+    sig = {
+        "lbrr_last_error": ([], C.c_char_p),
+        "lbrr_abi_version": ([], C.c_int),
+        "lbrr_default_model": ([C.POINTER(ModelDesc), C.POINTER(C.c_int32), i32], C.c_int),
+        "lbrr_engine_create": ([C.c_int, C.POINTER(ModelDesc), i64, C.POINTER(vp)], C.c_int),
+        "lbrr_engine_load_weights": ([vp, C.POINTER(WeightView), C.c_size_t], C.c_int),
+        "lbrr_engine_load_safetensors": ([vp, C.c_char_p], C.c_int),
+        "lbrr_forward_chunk": ([vp, vp, i64, vp, vp], C.c_int),
+        "lbrr_forward_chunk_host": ([vp, vp, i64, vp], C.c_int),
+        "lbrr_forward_trunk": ([vp, vp, i64, C.c_int, vp, vp], C.c_int),
+        "lbrr_engine_sync": ([vp], C.c_int),
+        "lbrr_engine_memory": ([vp, C.POINTER(i64), C.POINTER(i64)], C.c_int),
+        "lbrr_engine_destroy": ([vp], None),
+        "lbrr_separate_song": ([C.POINTER(vp), C.c_int, vp, i64, C.POINTER(ChunkPlan), vp], C.c_int),
+        "lbrr_op_norm_gates": ([vp, vp, vp, vp, vp, vp, i64, vp], C.c_int),
+        "lbrr_op_qkv_rope": ([vp, vp, vp, vp, vp, vp, i64, i32, i32, vp], C.c_int),
+        "lbrr_op_attention": ([vp, vp, vp, i64, i32, i32, vp], C.c_int),
+        "lbrr_op_outproj_norm": ([vp, vp, vp, vp, vp, vp, vp, i64, vp], C.c_int),
+        "lbrr_op_ff1_gelu": ([vp, vp, vp, vp, i64, vp], C.c_int),
+        "lbrr_op_ff2_resid": ([vp, vp, vp, vp, vp, i64, vp], C.c_int),
+        "lbrr_op_sync": ([vp], C.c_int),
+        "lbrr_f32_to_f16_bits": ([C.c_float], C.c_uint16),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+# Every symbol include/lbrr_gpu.h declares (checked by the CPU test suite).
+HEADER_SYMBOLS = [
+    "lbrr_last_error", "lbrr_abi_version", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
+    "lbrr_engine_load_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
+    "lbrr_engine_sync", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
+    "lbrr_op_qkv_rope", "lbrr_op_attention", "lbrr_op_outproj_norm", "lbrr_op_ff1_gelu", "lbrr_op_ff2_resid",
+    "lbrr_op_sync",
+]
+
+
+def check(rc: int):
+    if rc != OK:
+        raise LbrrError(rc, lib().lbrr_last_error().decode(errors="replace"))
+
+
+def _ptr(t):
+    """Device (or host) address of a torch tensor / numpy array; None -> NULL."""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        return None
+    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+
+
+def default_model():
+    d = ModelDesc()
+    freqs = (C.c_int32 * 62)()
+    check(lib().lbrr_default_model(C.byref(d), freqs, 62))
+    d._keep = freqs
+    return d
+
+
+class Engine:
+    """One GPU's engine: weights, scratch, cuFFT plans and a stream."""
+
+    def __init__(self, device: int = 0, max_chunk_samples: int = CHUNK):
+        self.device = device
+        self.max_chunk_samples = max_chunk_samples
+        h = C.c_void_p()
+        desc = default_model()
+        check(lib().lbrr_engine_create(device, C.byref(desc), max_chunk_samples, C.byref(h)))
+        self.handle = h
+
+    # -- weights -------------------------------------------------------------
+    def upload_weights(self, weights: dict):
+        """Validate and upload a checkpoint given as {name: fp32 array/tensor}
+        (ModelWeights::load + upload_weights, src/weights.rs:307-447, src/main.rs:6045-6077)."""
+        keep, views = [], (WeightView * len(weights))()
+        for i, (name, t) in enumerate(weights.items()):
+            a = np.ascontiguousarray(np.asarray(t.detach().cpu() if hasattr(t, "detach") else t, dtype=np.float32))
+            keep.append(a)
+            views[i].name = name.encode()
+            views[i].data = a.ctypes.data_as(C.POINTER(C.c_float))
+            views[i].numel = a.size
+        check(lib().lbrr_engine_load_weights(self.handle, views, len(weights)))
+
+    def load_safetensors(self, path):
+        check(lib().lbrr_engine_load_safetensors(self.handle, str(path).encode()))
+
+    # -- forward -------------------------------------------------------------
+    def bench_forward(self, x_dev, out_dev, stream=None):
+        """One chunk on device buffers: x [len][2] fp32 -> stems [6][2][len] fp32."""
+        length = x_dev.numel() // 2
+        check(lib().lbrr_forward_chunk(self.handle, _ptr(x_dev), length, _ptr(out_dev), _stream(stream)))
+
+    def forward_host(self, x_host: np.ndarray) -> np.ndarray:
+        """End to end from host memory: x [len][2] fp32 -> stems [6][2][len] fp32."""
+        x = np.ascontiguousarray(x_host, dtype=np.float32)
+        length = x.shape[0]
+        out = np.empty((STEMS, 2, length), dtype=np.float32)
+        check(lib().lbrr_forward_chunk_host(self.handle, x.ctypes.data, length, out.ctypes.data))
+        return out
+
+    def forward_trunk(self, x_dev, n_steps: int, x_out_dev, stream=None):
+        length = x_dev.numel() // 2
+        check(lib().lbrr_forward_trunk(self.handle, _ptr(x_dev), length, n_steps, _ptr(x_out_dev), _stream(stream)))
+
+    def sync(self):
+        check(lib().lbrr_engine_sync(self.handle))
+
+    def memory(self):
+        w, s = C.c_int64(), C.c_int64()
+        check(lib().lbrr_engine_memory(self.handle, C.byref(w), C.byref(s)))
+        return w.value, s.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().lbrr_engine_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def separate(engines, audio_planar: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER) -> np.ndarray:
+    """Whole-song demix over one or more engines (separate(), src/main.rs:7598-7819).
+    audio_planar: [2][len] fp32 -> stems [6][2][len] fp32."""
+    x = np.ascontiguousarray(np.asarray(audio_planar, dtype=np.float32).T)
+    length = x.shape[0]
+    out = np.empty((STEMS, 2, length), dtype=np.float32)
+    hs = (C.c_void_p * len(engines))(*[e.handle for e in engines])
+    plan = ChunkPlan(chunk, step, border)
+    check(lib().lbrr_separate_song(hs, len(engines), x.ctypes.data, length, C.byref(plan), out.ctypes.data))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Per-op entry points (torch CUDA tensors; fp16 tensors are torch.float16)
+# ---------------------------------------------------------------------------
+def op_sync(stream=None):
+    check(lib().lbrr_op_sync(_stream(stream)))
+
+
+def norm_gates(x, gamma, gate_w, gate_b, h16, gates, stream=None):
+    check(lib().lbrr_op_norm_gates(_ptr(x), _ptr(gamma), _ptr(gate_w), _ptr(gate_b), _ptr(h16), _ptr(gates),
+                                   x.shape[0], _stream(stream)))
+
+
+def qkv_rope(h16, w16, bias16, cos, sin, qkv, frames, bands, axis, stream=None):
+    check(lib().lbrr_op_qkv_rope(_ptr(h16), _ptr(w16), _ptr(bias16), _ptr(cos), _ptr(sin), _ptr(qkv), frames, bands,
+                                 axis, _stream(stream)))
+
+
+def attention(qkv, gates, out, frames, bands, axis, stream=None):
+    check(lib().lbrr_op_attention(_ptr(qkv), _ptr(gates), _ptr(out), frames, bands, axis, _stream(stream)))
+
+
+def outproj_norm(scaled16, w16, bias, resid, gamma, attn_out, h16, stream=None):
+    check(lib().lbrr_op_outproj_norm(_ptr(scaled16), _ptr(w16), _ptr(bias), _ptr(resid), _ptr(gamma), _ptr(attn_out),
+                                     _ptr(h16), scaled16.shape[0], _stream(stream)))
+
+
+def ff1_gelu(h16, w16, b1, ff1, stream=None):
+    check(lib().lbrr_op_ff1_gelu(_ptr(h16), _ptr(w16), _ptr(b1), _ptr(ff1), h16.shape[0], _stream(stream)))
+
+
+def ff2_resid(ff1, w16, b2, resid, x, stream=None):
+    check(lib().lbrr_op_ff2_resid(_ptr(ff1), _ptr(w16), _ptr(b2), _ptr(resid), _ptr(x), ff1.shape[0],
+                                  _stream(stream)))
+
+
+def f32_to_f16_bits(v: float) -> int:
+    return int(lib().lbrr_f32_to_f16_bits(C.c_float(v)))

@@ -1,0 +1,128 @@
+"""Per-op parity on the GPU: each C-ABI entry point against the CPU oracle.
+
+Inputs are seeded; fp16 operands are exact fp16 values on both sides, so the
+only differences are accumulation order (fp32 on the tensor cores vs the CPU)
+and the occasional fp16 rounding flip that causes.  Tolerances are written per
+test: relative L2 error, and max abs error against the output scale.
+"""
+import numpy as np
+import pytest
+import torch
+
+from helpers import f16, fold, oracle_attention_gated, randn, rel_err, snr_db, unfold
+from oracle import bsroformer_ref as R
+
+pytestmark = pytest.mark.gpu
+
+NB = 62
+
+
+@pytest.fixture(scope="module")
+def lb():
+    import lbrr
+    lbrr.lib()
+    return lbrr
+
+
+def cuda(t, dtype=None):
+    return t.to(dtype or t.dtype).contiguous().cuda()
+
+
+@pytest.mark.parametrize("M", [62, 2294, 71362])
+def test_norm_gates(lb, M):
+    x = randn((M, 256), 1, 0.7)
+    gamma = 1.0 + randn((256,), 2, 0.1)
+    gw, gb = randn((8, 256), 3, 0.05), randn((8,), 4, 0.05)
+    h16 = torch.empty(M, 256, dtype=torch.float16, device="cuda")
+    gates = torch.empty(M, 8, device="cuda")
+    lb.norm_gates(cuda(x), cuda(gamma), cuda(gw), cuda(gb), h16, gates)
+    lb.op_sync()
+    hf = R.rmsnorm(x, gamma, "right")
+    assert rel_err(h16.float().cpu(), f16(hf)) < 2e-3
+    assert rel_err(gates.cpu(), hf @ gw.T + gb) < 1e-5
+
+
+@pytest.mark.parametrize("T,axis", [(1, 0), (37, 0), (259, 0), (1, 1), (37, 1)])
+def test_qkv_rope(lb, T, axis):
+    M = T * NB
+    h = f16(randn((M, 256), 10 + T, 1.0))
+    w = f16(randn((1536, 256), 11, 0.02))
+    bias16 = f16(randn((1536,), 12, 0.02))
+    P = T if axis == 0 else NB
+    cos, sin = R.rope_tables(P)
+    qkv = torch.empty(M, 1536, dtype=torch.float16, device="cuda")
+    lb.qkv_rope(cuda(h, torch.float16), cuda(w, torch.float16), cuda(bias16), cuda(cos), cuda(sin), qkv, T, NB, axis)
+    lb.op_sync()
+    ref = f16(h @ w.T + bias16)
+    q, k, v = ref[:, :512], ref[:, 512:1024], ref[:, 1024:]
+    qr = unfold(f16(R.rope(fold(q, T, NB, axis), cos, sin)), T, NB, axis)
+    kr = unfold(f16(R.rope(fold(k, T, NB, axis), cos, sin)), T, NB, axis)
+    got = qkv.float().cpu()
+    for sl, r in ((slice(0, 512), qr), (slice(512, 1024), kr), (slice(1024, 1536), v)):
+        assert rel_err(got[:, sl], r) < 2e-3
+        assert float((got[:, sl] - r).abs().max()) <= 4e-3 * float(r.abs().max())
+
+
+@pytest.mark.parametrize("T,axis", [(1, 0), (37, 0), (129, 0), (259, 0), (1, 1), (2, 1), (37, 1)])
+def test_attention(lb, T, axis):
+    M = T * NB
+    qkv = f16(randn((M, 1536), 20 + T, 1.0))
+    gates = randn((M, 8), 21, 1.0)
+    out = torch.empty(M, 512, dtype=torch.float16, device="cuda")
+    lb.attention(cuda(qkv, torch.float16), cuda(gates), out, T, NB, axis)
+    lb.op_sync()
+    ref = oracle_attention_gated(qkv, gates, T, NB, axis)
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert snr_db(got, ref) > 55.0, snr_db(got, ref)
+
+
+@pytest.mark.parametrize("M", [62, 2294, 16058])
+def test_outproj_norm(lb, M):
+    s = f16(randn((M, 512), 30, 0.5))
+    w = f16(randn((256, 512), 31, 0.02))
+    bias = randn((256,), 32, 0.02)
+    x = randn((M, 256), 33, 1.0)
+    gamma = 1.0 + randn((256,), 34, 0.1)
+    ao = torch.empty(M, 256, device="cuda")
+    h16 = torch.empty(M, 256, dtype=torch.float16, device="cuda")
+    lb.outproj_norm(cuda(s, torch.float16), cuda(w, torch.float16), cuda(bias), cuda(x), cuda(gamma), ao, h16)
+    lb.op_sync()
+    ref = s @ w.T + bias + x
+    assert rel_err(ao.cpu(), ref) < 1e-5
+    assert rel_err(h16.float().cpu(), f16(R.rmsnorm(ref, gamma, "left"))) < 2e-3
+
+
+@pytest.mark.parametrize("M", [1, 37, 127, 129, 16058, 71362])
+def test_ff1_gelu(lb, M):
+    # the M list of the reference's FF1 regression (src/main.rs:8024)
+    h = f16(randn((M, 256), 40, 1.0))
+    w = f16(randn((1024, 256), 41, 0.05))
+    b = randn((1024,), 42, 0.05)
+    out = torch.empty(M, 1024, dtype=torch.float16, device="cuda")
+    lb.ff1_gelu(cuda(h, torch.float16), cuda(w, torch.float16), cuda(b), out)
+    lb.op_sync()
+    ref = f16(R.gelu_as(h @ w.T + b))
+    got = out.float().cpu()
+    assert rel_err(got, ref) < 2e-3
+    assert float((got - ref).abs().max()) <= 4e-3 * float(ref.abs().max())
+
+
+@pytest.mark.parametrize("M", [1, 129, 16058])
+def test_ff2_resid(lb, M):
+    f = f16(randn((M, 1024), 50, 0.5))
+    w = f16(randn((256, 1024), 51, 0.02))
+    b = randn((256,), 52, 0.02)
+    r = randn((M, 256), 53, 1.0)
+    x = torch.empty(M, 256, device="cuda")
+    lb.ff2_resid(cuda(f, torch.float16), cuda(w, torch.float16), cuda(b), cuda(r), x)
+    lb.op_sync()
+    assert rel_err(x.cpu(), f @ w.T + b + r) < 1e-5
+
+
+def test_invalid_arguments_are_rejected(lb):
+    with pytest.raises(lb.LbrrError) as ei:
+        lb.check(lb.lib().lbrr_op_attention(None, None, None, 10, 62, 0, None))
+    assert ei.value.code == lb.ERR_INVALID
+    with pytest.raises(lb.LbrrError):
+        lb.check(lb.lib().lbrr_op_attention(1, 1, 1, 10, 100, 1, None))  # freq axis needs bands <= 64
