@@ -1,0 +1,457 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 BS-RoFormer engine (the driver's bench contract).
+
+Workload: one 588800-sample stereo chunk (T = 1151
+frames, M = 71362 tokens) through the full 12-layer, 6-stem model, from the
+STFT to the ISTFT overlap-add waveform, seeded synthetic audio and random-init
+weights (N(0, 0.02), gammas 1).  A "step" is one chunk per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value       aggregate ms per chunk over all GPUs (device time, CUDA events on the
+            engine stream, max over ranks; lower is better); L2 is flushed
+            between steps (256 MiB write outside the events)
+e2e         the same metric through the host entry point lbrr_forward_chunk_host
+            (pinned staging, H2D of the chunk, forward, D2H of the 6 stems)
+roofline    dominant kernel (time-axis attention) timed live on its own stream
+            with CUDA events at full size: algorithmic FLOP / duration vs the
+            measured dense tensor peak in MEASURED_PEAKS.json
+cpu_baseline  the CPU oracle (PyTorch fp32 restatement; the reference has no
+            CPU path) on a bounded sample, extrapolated to one chunk
+song        whole-song RTF (180.48 s, reference chunk plan)
+            at N GPUs: chunks dealt round-robin, per-chunk waveforms gathered to
+            rank 0 over NCCL and accumulated there in chunk order
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "logic-bs-roformer-rs_b200"))
+
+CHUNK = 588800
+SONG_LEN = 7959168  # 180.48 s at 44.1 kHz
+SR = 44100
+METRIC = "ms/588800-sample chunk"
+UNIT = "ms/chunk"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "tflops_sustained": d["bf16_tflops_sustained"],
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi sampling during the timed region (SM clock, reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"lbrr_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        if self.path.exists():
+            for line in self.path.read_text().splitlines():
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def make_inputs(seed=0):
+    from oracle import bsroformer_ref as R
+    return R.make_weights(seed=0), R.synth_audio(CHUNK, seed=seed)
+
+
+def time_dominant_kernel(torch, lbrr, T=1151, iters=10):
+    """Time-axis attention at the bench size on its own stream: FLOP = 4*62*8*T^2*64."""
+    M = T * 62
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkv = torch.randn(M, 1536, device="cuda", generator=g).half()
+    gates = torch.randn(M, 8, device="cuda", generator=g)
+    out = torch.empty(M, 512, device="cuda", dtype=torch.float16)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            lbrr.attention(qkv, gates, out, T, 62, 0, stream=s)
+        s.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+        for a, b in ev:
+            a.record(s)
+            lbrr.attention(qkv, gates, out, T, 62, 0, stream=s)
+            b.record(s)
+        s.synchronize()
+    lbrr.op_sync(s)
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    flop = 4 * 62 * 8 * T * T * 64
+    return ms, flop
+
+
+def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
+    """Per-GEMM tensor throughput at M = 62*T (QKV, out-proj, FF1, FF2)."""
+    M = T * 62
+    g = torch.Generator(device="cuda").manual_seed(1)
+    h = torch.randn(M, 256, device="cuda", generator=g).half()
+    w_qkv = (torch.randn(1536, 256, device="cuda", generator=g) * 0.02).half()
+    b16 = torch.zeros(1536, device="cuda")
+    cos = torch.ones(T, 32, device="cuda")
+    sin = torch.zeros(T, 32, device="cuda")
+    qkv = torch.empty(M, 1536, device="cuda", dtype=torch.float16)
+    sc = torch.randn(M, 512, device="cuda", generator=g).half()
+    wo = (torch.randn(256, 512, device="cuda", generator=g) * 0.02).half()
+    bo = torch.zeros(256, device="cuda")
+    x = torch.randn(M, 256, device="cuda", generator=g)
+    gam = torch.ones(256, device="cuda")
+    ao = torch.empty(M, 256, device="cuda")
+    h2 = torch.empty(M, 256, device="cuda", dtype=torch.float16)
+    w1 = (torch.randn(1024, 256, device="cuda", generator=g) * 0.02).half()
+    b1 = torch.zeros(1024, device="cuda")
+    ff1 = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
+    w2 = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
+    xo = torch.empty(M, 256, device="cuda")
+    cases = {
+        "qkv": (lambda s: lbrr.qkv_rope(h, w_qkv, b16, cos, sin, qkv, T, 62, 0, stream=s), 2 * M * 1536 * 256),
+        "out_proj": (lambda s: lbrr.outproj_norm(sc, wo, bo, x, gam, ao, h2, stream=s), 2 * M * 256 * 512),
+        "ff1": (lambda s: lbrr.ff1_gelu(h, w1, b1, ff1, stream=s), 2 * M * 1024 * 256),
+        "ff2": (lambda s: lbrr.ff2_resid(ff1, w2, bo, x, xo, stream=s), 2 * M * 256 * 1024),
+    }
+    res = {}
+    s = torch.cuda.Stream()
+    for name, (fn, flop) in cases.items():
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn(s)
+            s.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+            for a, b in ev:
+                a.record(s)
+                fn(s)
+                b.record(s)
+            s.synchronize()
+        lbrr.op_sync(s)
+        ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+        res[name] = {"ms": round(ms, 4), "tflops": round(flop / ms / 1e9, 1)}
+    return res
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import lbrr
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    pk = peaks()
+    weights, audio = make_inputs(seed=rank)
+    eng = lbrr.Engine(local_rank, CHUNK)
+    eng.upload_weights(weights)
+    del weights
+    x = torch.from_numpy(np.ascontiguousarray(audio.T)).cuda()
+    out = torch.empty(6, 2, CHUNK, device="cuda")
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device="cuda")  # 256 MiB > 126 MB L2
+    stream = torch.cuda.Stream()
+
+    def step():
+        eng.bench_forward(x, out, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        stream.synchronize()
+    eng.sync()
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    # ---- device-timed region ----
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        with torch.cuda.stream(stream):
+            for a, b in evs:
+                a.record(stream)
+                step()
+                b.record(stream)
+                flush.fill_(1.0)  # outside the events: evicts L2 between steps
+        torch.cuda.synchronize()
+        barrier()
+    eng.sync()
+    step_ms = [a.elapsed_time(b) for a, b in evs]
+    ms = sum(step_ms) / len(step_ms)
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = clk.summary()
+
+    # ---- end to end through the host entry point ----
+    xh = np.ascontiguousarray(audio.T)
+    eng.forward_host(xh)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.forward_host(xh)
+    e2e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    if dist:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    # ---- whole song at N GPUs ----
+    song = run_song(torch, lbrr, eng, rank, world, dist)
+
+    result = None
+    if rank == 0:
+        attn_ms, attn_flop = time_dominant_kernel(torch, lbrr)
+        gemms = time_trunk_gemms(torch, lbrr)
+        achieved = attn_flop / attn_ms / 1e9  # TFLOP/s
+        traffic = None
+        tf = ROOT / "profiles" / "attn_time_T1151_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("bytes_per_launch")
+        for g in gemms.values():
+            g["pct_of_peak"] = round(100.0 * g["tflops"] / pk["tflops"], 1)
+        wb, sb = eng.memory()
+        result = {
+            "metric": METRIC, "value": round(ms / world, 4), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic (seeded sines + noise; random-init weights N(0,0.02))",
+            "config": {"workload": "full chunk 588800 samples (T=1151, M=71362), 12 layers, 6 stems, waveform out",
+                       "global_batch": world, "seq_len": 1151, "parallelism": f"chunks dealt over {world} GPU(s)",
+                       "l2": "flushed between steps (256 MiB write outside the timed events)"},
+            "e2e": {"value": round(e2e_ms / world, 4), "unit": UNIT, "h2d_bytes_per_step": CHUNK * 2 * 4 * world,
+                    "d2h_bytes_per_step": 6 * 2 * CHUNK * 4 * world},
+            "gpu_launches": 151 * args.steps * world,
+            "roofline": {"kernel": "attention time axis (attn_kernel, T=1151, 496 sequences)", "bound": "tensor",
+                         "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
+                         "frac": round(achieved / pk["tflops"], 4), "traffic": traffic,
+                         "peak_source": pk["source"] + " dense bf16 burst (MEASURED_PEAKS.json)"},
+            "trunk_gemms": gemms,
+            "chunk_rtf": round(ms / (CHUNK / SR * 1000.0), 6),
+            "song": song,
+            "clocks": clocks,
+            "memory_bytes": {"weights": wb, "scratch": sb},
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_baseline_sample()
+    eng.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def run_song(torch, lbrr, eng, rank, world, dist):
+    """180.48 s song, reference chunk plan (15 chunks).  1 GPU: lbrr_separate_song.
+    N GPUs: chunk i on rank i % N, waveforms gathered to rank 0 (NCCL), accumulated
+    there in chunk order with the same fade/normalisation as the single-GPU path."""
+    from oracle import bsroformer_ref as R
+    audio = R.synth_audio(SONG_LEN, seed=42)
+    starts = R.chunk_starts(SONG_LEN)
+    if world == 1:
+        lbrr.separate([eng], audio)  # warm
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        lbrr.separate([eng], audio)
+        dt = time.perf_counter() - t0
+        return {"seconds": round(dt, 4), "audio_seconds": SONG_LEN / SR, "rtf": round(dt / (SONG_LEN / SR), 6),
+                "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440"}
+    # multi-rank: each rank forwards its chunks; rank 0 receives and stitches
+    needed = R.BORDER + SONG_LEN
+    xp = R.reflect_pad(audio, R.BORDER, starts[-1] + R.CHUNK - needed)
+    buf = torch.empty(6, 2, R.CHUNK, device="cuda")
+    recv = torch.empty(6, 2, R.CHUNK, device="cuda")
+    fade = torch.from_numpy(R.fade_window()).cuda()
+    dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    result = torch.zeros(12, needed, device="cuda") if rank == 0 else None
+    counter = torch.zeros(needed, device="cuda") if rank == 0 else None
+    for i, s in enumerate(starts):
+        owner = i % world
+        if owner == rank:
+            xin = torch.from_numpy(np.ascontiguousarray(xp[:, s:s + R.CHUNK].T)).cuda()
+            eng.bench_forward(xin, buf)
+            eng.sync()
+            if rank != 0:
+                dist.send(buf, dst=0)
+        if rank == 0:
+            y = buf if owner == 0 else recv
+            if owner != 0:
+                dist.recv(recv, src=owner)
+            w = fade.clone()
+            if i == 0:
+                w[:R.BORDER] = 1
+            if i == len(starts) - 1:
+                w[-R.BORDER:] = 1
+            take = min(R.CHUNK, needed - s)
+            result[:, s:s + take] += y.reshape(12, -1)[:, :take] * w[:take]
+            counter[s:s + take] += w[:take] * w[:take]
+    if rank == 0:
+        out = (result / counter.clamp_min(1e-8))[:, R.BORDER:needed]
+        out.cpu()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    t = torch.tensor([dt], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dt = float(t.item())
+    return {"seconds": round(dt, 4), "audio_seconds": SONG_LEN / SR, "rtf": round(dt / (SONG_LEN / SR), 6),
+            "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440",
+            "exchange": "per-chunk waveform [6][2][588800] fp32 sent to rank 0 over NCCL"}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port) and the reference arm
+# ---------------------------------------------------------------------------
+def cpu_sample_ms(torch):
+    """Front end + one layer (time + freq axis) + mask estimator + ISTFT of the full
+    chunk on the CPU oracle in fp32; returns ms extrapolated to the 12-layer chunk."""
+    from oracle import bsroformer_ref as R
+    w = R.make_weights(seed=0)
+    o = R.Oracle(w, "fp32")
+    audio = torch.from_numpy(R.synth_audio(CHUNK, seed=0))
+    T = R.num_frames(CHUNK)
+    with torch.inference_mode():
+        t0 = time.perf_counter()
+        spec = R.stft(audio)
+        x = o.band_split(R.spec_reorder(spec))
+        t1 = time.perf_counter()
+        x = o.trunk(x, T, layers=1)
+        t2 = time.perf_counter()
+        xf = R.rmsnorm(x, w["final_norm.gamma"], "left")
+        masks = o.mask_estimator(xf, T)
+        y = R.istft(o.mask_apply(spec, masks).reshape(12, T, R.FREQ_BINS), CHUNK)
+        t3 = time.perf_counter()
+    assert torch.isfinite(y).all()
+    front_back = (t1 - t0) + (t3 - t2)
+    layer = t2 - t1
+    return (front_back + R.DEPTH * layer) * 1000.0, (t3 - t0)
+
+
+def cpu_baseline_sample():
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    ms, sample_s = cpu_sample_ms(torch)
+    return {"value": round(ms, 1), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"CPU oracle fp32 (PyTorch restatement of the reference forward): front end + 1 of 12 "
+                      f"layers + mask estimator + ISTFT of one 588800-sample chunk ({sample_s:.1f} s), "
+                      f"extrapolated to 12 layers"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    for _ in range(args.warmup):
+        cpu_sample_ms(torch)
+    vals = []
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ms, sample_s = cpu_sample_ms(torch)
+        vals.append(ms)
+    ms = statistics.mean(vals)
+    return {"impl": "reference", "metric": METRIC, "value": round(ms, 1), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded sines + noise; random-init weights N(0,0.02))",
+            "config": {"workload": "full chunk 588800 samples (T=1151, M=71362), 12 layers, 6 stems, waveform out",
+                       "global_batch": 1, "seq_len": 1151, "parallelism": "CPU host threads"},
+            "cpu_baseline": {"value": round(ms, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": "CPU oracle fp32: front end + 1 layer + mask estimator + ISTFT per step, "
+                                       "extrapolated to 12 layers (the reference has no CPU path; its GPU code "
+                                       "needs the absent cuda-oxide toolchain)"},
+            "e2e": {"value": round(ms, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": round(time.perf_counter() - t0, 1)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        res = run_ours(args, rank, world, local_rank)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

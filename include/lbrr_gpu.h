@@ -115,6 +115,14 @@ int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, fl
 int lbrr_forward_trunk(lbrr_engine* e, const float* x_dev, int64_t len, int n_steps, float* x_out_dev,
                        void* stream);
 
+/* Copy an internal buffer of the last forward to host memory (after syncing the
+ * engine stream): "spec" [2][T][1025] complex64, "c2r" (masked spectra)
+ * [12][T][1025] complex64, "pcm" [12][T][2048] fp32, "x" [T*62][256] fp32,
+ * "xb16" [62][T][256] fp16, "hidden" [6*62][T][1024] fp16.  `bytes` must not
+ * exceed the buffer's size for the current length.  Diagnostic taps like the
+ * reference's --dump-trunk dumps (src/main.rs:7055-7150). */
+int lbrr_engine_read_buffer(lbrr_engine* e, const char* name, void* host_dst, int64_t bytes);
+
 /* Synchronise the engine stream and check the device status word. */
 int lbrr_engine_sync(lbrr_engine* e);
 

@@ -769,6 +769,28 @@ static int check_status(int* status_dev, cudaStream_t st) {
   return LBRR_OK;
 }
 
+extern "C" int lbrr_engine_read_buffer(lbrr_engine* e, const char* name, void* dst, int64_t bytes) {
+  if (!e || !name || !dst || bytes < 0) return fail(LBRR_ERR_INVALID, "NULL argument");
+  if (e->cur_T <= 0) return fail(LBRR_ERR_STATE, "no forward has run yet");
+  DeviceGuard g(e->device);
+  const size_t T = e->cur_T, M = T * kNumBands;
+  const void* src = nullptr;
+  size_t cap = 0;
+  const std::string n(name);
+  if (n == "spec") src = e->spec, cap = 2 * T * kBins * sizeof(float2);
+  else if (n == "c2r") src = e->c2r, cap = 2 * kStems * T * kBins * sizeof(float2);
+  else if (n == "pcm") src = e->pcm, cap = 2 * kStems * T * kNfft * sizeof(float);
+  else if (n == "x") src = e->x, cap = M * 256 * sizeof(float);
+  else if (n == "xb16") src = e->xb16, cap = M * 256 * sizeof(__half);
+  else if (n == "hidden") src = e->hidden, cap = kStems * M * 1024 * sizeof(__half);
+  else return fail(LBRR_ERR_INVALID, "unknown buffer " + n);
+  if (static_cast<size_t>(bytes) > cap) return fail(LBRR_ERR_INVALID, "read exceeds the buffer");
+  CK(cudaStreamSynchronize(e->stream));
+  CK(cudaDeviceSynchronize());
+  CK(cudaMemcpy(dst, src, static_cast<size_t>(bytes), cudaMemcpyDeviceToHost));
+  return LBRR_OK;
+}
+
 extern "C" int lbrr_engine_sync(lbrr_engine* e) {
   if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
   DeviceGuard g(e->device);

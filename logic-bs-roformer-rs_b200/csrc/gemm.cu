@@ -341,7 +341,10 @@ struct EpiMask : TableTiles {
             const float mr = m[2 * ch], mi = m[2 * ch + 1];
             float2 o;
             o.x = s.x * mr - s.y * mi;
-            o.y = s.x * mi + s.y * mr;
+            // A real signal's DC and Nyquist bins are real: torch.istft drops
+            // their imaginary parts, and cuFFT's C2R is only defined for such
+            // Hermitian input, so the masked spectrum keeps them real.
+            o.y = (f == 0 || f == 1024) ? 0.f : s.x * mi + s.y * mr;
             out[(static_cast<size_t>(stem * 2 + ch) * T + r) * 1025 + f] = o;
           }
         }

@@ -74,6 +74,7 @@ def lib() -> C.CDLL:
         "lbrr_forward_chunk_host": ([vp, vp, i64, vp], C.c_int),
         "lbrr_forward_trunk": ([vp, vp, i64, C.c_int, vp, vp], C.c_int),
         "lbrr_engine_sync": ([vp], C.c_int),
+        "lbrr_engine_read_buffer": ([vp, C.c_char_p, vp, i64], C.c_int),
         "lbrr_engine_memory": ([vp, C.POINTER(i64), C.POINTER(i64)], C.c_int),
         "lbrr_engine_destroy": ([vp], None),
         "lbrr_separate_song": ([C.POINTER(vp), C.c_int, vp, i64, C.POINTER(ChunkPlan), vp], C.c_int),
@@ -98,7 +99,7 @@ def lib() -> C.CDLL:
 HEADER_SYMBOLS = [
     "lbrr_last_error", "lbrr_abi_version", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
     "lbrr_engine_load_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
-    "lbrr_engine_sync", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
+    "lbrr_engine_sync", "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
     "lbrr_op_qkv_rope", "lbrr_op_attention", "lbrr_op_outproj_norm", "lbrr_op_ff1_gelu", "lbrr_op_ff2_resid",
     "lbrr_op_sync",
 ]
@@ -179,6 +180,12 @@ class Engine:
 
     def sync(self):
         check(lib().lbrr_engine_sync(self.handle))
+
+    def read_buffer(self, name: str, shape, dtype) -> np.ndarray:
+        """Host copy of an internal buffer of the last forward (diagnostic tap)."""
+        out = np.empty(shape, dtype=dtype)
+        check(lib().lbrr_engine_read_buffer(self.handle, name.encode(), out.ctypes.data, out.nbytes))
+        return out
 
     def memory(self):
         w, s = C.c_int64(), C.c_int64()
