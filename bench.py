@@ -432,6 +432,82 @@ def run_reference(args, rank, world):
             "wall_s": round(time.perf_counter() - t0, 1)}
 
 
+def run_forward_only(args):
+    """Profiling driver: warmup + timed chunk forwards only (for ncu launch lists)."""
+    import torch
+    import lbrr
+    weights, audio = make_inputs(seed=0)
+    L = args.frames * 512 - 1 if args.frames else CHUNK
+    eng = lbrr.Engine(0, max(L, 4096))
+    eng.upload_weights(weights)
+    x = torch.from_numpy(np.ascontiguousarray(audio[:, :L].T)).cuda()
+    out = torch.empty(6, 2, L, device="cuda")
+    for _ in range(args.warmup):
+        eng.bench_forward(x, out)
+    eng.sync()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.bench_forward(x, out)
+    eng.sync()
+    ms = (time.perf_counter() - t0) * 1000.0 / max(1, args.steps)
+    print(json.dumps({"mode": "forward-only", "len": L, "ms_per_chunk_wall": round(ms, 3)}))
+    eng.close()
+
+
+def run_op(args):
+    """Profiling driver: one kernel at a chosen size (e.g. --op attn_time --frames 259)."""
+    import torch
+    import lbrr
+    T = args.frames or 1151
+    M = T * 62
+    g = torch.Generator(device="cuda").manual_seed(0)
+    if args.op in ("attn_time", "attn_freq"):
+        qkv = torch.randn(M, 1536, device="cuda", generator=g).half()
+        gates = torch.randn(M, 8, device="cuda", generator=g)
+        out = torch.empty(M, 512, device="cuda", dtype=torch.float16)
+        axis = 0 if args.op == "attn_time" else 1
+        fn = lambda: lbrr.attention(qkv, gates, out, T, 62, axis)  # noqa: E731
+    else:
+        h = torch.randn(M, 256, device="cuda", generator=g).half()
+        if args.op == "qkv":
+            w = (torch.randn(1536, 256, device="cuda", generator=g) * 0.02).half()
+            b = torch.zeros(1536, device="cuda")
+            c, s = torch.ones(T, 32, device="cuda"), torch.zeros(T, 32, device="cuda")
+            o = torch.empty(M, 1536, device="cuda", dtype=torch.float16)
+            fn = lambda: lbrr.qkv_rope(h, w, b, c, s, o, T, 62, 0)  # noqa: E731
+        elif args.op == "ff1":
+            w = (torch.randn(1024, 256, device="cuda", generator=g) * 0.02).half()
+            b = torch.zeros(1024, device="cuda")
+            o = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
+            fn = lambda: lbrr.ff1_gelu(h, w, b, o)  # noqa: E731
+        elif args.op == "ff2":
+            f = torch.randn(M, 1024, device="cuda", generator=g).half()
+            w = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
+            b = torch.zeros(256, device="cuda")
+            r = torch.randn(M, 256, device="cuda", generator=g)
+            o = torch.empty(M, 256, device="cuda")
+            fn = lambda: lbrr.ff2_resid(f, w, b, r, o)  # noqa: E731
+        else:  # outproj
+            sc = torch.randn(M, 512, device="cuda", generator=g).half()
+            w = (torch.randn(256, 512, device="cuda", generator=g) * 0.02).half()
+            b = torch.zeros(256, device="cuda")
+            r = torch.randn(M, 256, device="cuda", generator=g)
+            o = torch.empty(M, 256, device="cuda")
+            h2 = torch.empty(M, 256, device="cuda", dtype=torch.float16)
+            fn = lambda: lbrr.outproj_norm(sc, w, b, r, torch.ones(256, device="cuda"), o, h2)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    lbrr.op_sync()
+    print(json.dumps({"mode": "op", "op": args.op, "frames": T, "ms": round(a.elapsed_time(e) / max(1, args.steps), 4)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -439,7 +515,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--forward-only", action="store_true", help="profiling: chunk forwards only")
+    ap.add_argument("--op", choices=["attn_time", "attn_freq", "qkv", "outproj", "ff1", "ff2"],
+                    help="profiling: run one kernel")
+    ap.add_argument("--frames", type=int, default=0, help="profiling: frames T (default 1151)")
     args = ap.parse_args()
+    if args.forward_only:
+        return run_forward_only(args)
+    if args.op:
+        return run_op(args)
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     rank = int(os.environ.get("RANK", "0"))

@@ -682,6 +682,18 @@ static int setup_length(lbrr_engine* e, int64_t len) {
     if (_e != cudaSuccess) return fail(LBRR_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(_e)); \
   } while (0)
 
+// Pre-attention RMSNorm + gates of step k, fused into the producing GEMM epilogue.
+static RowNorm attn_norm(lbrr_engine* e, int k) {
+  RowNorm n;
+  n.kind = 2;
+  n.gamma = e->steps[k].norm_g;
+  n.gate_w = e->steps[k].gate_w;
+  n.gate_b = e->steps[k].gate_b;
+  n.h16 = e->h16;
+  n.gates = e->gates;
+  return n;
+}
+
 static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t st) {
   const BandGeom& G = geom();
   const int T = e->cur_T;
@@ -689,28 +701,40 @@ static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t s
   CKFFT(cufftSetStream(e->plan_r2c, st));
   CKFFT(cufftExecR2C(e->plan_r2c, e->frames, reinterpret_cast<cufftComplex*>(e->spec)));
   CKL(band_norm(e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols, T, kNumBands, st));
+  // band split, fused with step 0's pre-attention RMSNorm + gates
   CKL(gemm_bandsplit(e->xn, G.xn_cols, e->band_w, G.kpad_max, e->band_b, e->x, T, kNumBands, e->tiles_band,
-                     e->n_band, e->status, st));
+                     e->n_band, attn_norm(e, 0), e->status, st));
   return LBRR_OK;
 }
 
+// h16 + gates of step k come from the epilogue that produced x (band split or
+// the previous step's FF2); after the last step that epilogue writes the final
+// norm in band-major order instead.
 static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
   const int T = e->cur_T, M = T * kNumBands, axis = k & 1;
   const StepWeights& w = e->steps[k];
-  CKL(norm_gates(e->x, w.norm_g, w.gate_w, w.gate_b, e->h16, e->gates, M, st));
   CKL(gemm_qkv(e->h16, w.wqkv, e->qkv_bias16, axis == 0 ? e->cos_t : e->cos_f, axis == 0 ? e->sin_t : e->sin_f,
                e->qkv, M, kNumBands, axis, e->status, st));
   CKL(attention_fwd(e->qkv, e->gates, e->scaled, T, kNumBands, axis, e->status, st));
   CKL(gemm_outproj_norm(e->scaled, w.wo, e->out_bias, e->x, w.ff_g, e->attn_out, e->h16, M, e->status, st));
   CKL(gemm_ff1_gelu(e->h16, w.w1, w.b1, e->ff1, M, e->status, st));
-  CKL(gemm_ff2_resid(e->ff1, w.w2, w.b2, e->attn_out, e->x, M, e->status, st));
+  RowNorm next;
+  if (k + 1 < 2 * kDepth) {
+    next = attn_norm(e, k + 1);
+  } else {
+    next.kind = 3;
+    next.gamma = e->final_g;
+    next.xb16 = e->xb16;
+    next.T = T;
+    next.nb = kNumBands;
+  }
+  CKL(gemm_ff2_resid(e->ff1, w.w2, w.b2, e->attn_out, e->x, M, next, e->status, st));
   return LBRR_OK;
 }
 
 static int run_back(lbrr_engine* e, int64_t len, float* out, cudaStream_t st) {
   const BandGeom& G = geom();
   const int T = e->cur_T;
-  CKL(final_norm_bandmajor(e->x, e->final_g, e->xb16, T, kNumBands, st));
   CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, T, kStems * kNumBands, e->tiles_m1, e->n_m1, e->status,
                  st));
   CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
@@ -1068,7 +1092,7 @@ extern "C" int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const
     return fail(LBRR_ERR_INVALID, "lbrr_op_ff2_resid: bad arguments");
   OP_PROLOGUE
   CK(gemm_ff2_resid(reinterpret_cast<const __half*>(ff1), reinterpret_cast<const __half*>(w16), b2, resid, x,
-                    static_cast<int>(rows), status, st));
+                    static_cast<int>(rows), RowNorm(), status, st));
   return LBRR_OK;
 }
 

@@ -1,16 +1,20 @@
 // tcgen05 GEMMs of the BS-RoFormer forward.
 //
-// One kernel template computes D[128 x n] = A[128 x K] * B[n x K]^T per CTA
-// tile with fp16 operands (both K-major, 128-byte swizzled, fed by TMA) and an
-// fp32 accumulator in TMEM.  Warp roles (192 threads):
-//   warp 0      TMA producer (one lane) over a STAGES-deep smem ring
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2..5  epilogue: one accumulator row per thread (tcgen05.ld 32x32b),
-//               fused per use (bias, RoPE, residual, RMSNorm, GELU, tanh, GLU,
-//               complex mask application).
+// One persistent kernel template computes, for every 128 x n output tile,
+// D = A[128 x K] * B[n x K]^T with fp16 operands (both K-major, 128-byte
+// swizzled, fed by TMA) and an fp32 accumulator in TMEM.  One CTA per SM
+// walks the tile list with a static stride.  Warp roles (320 threads):
+//   warp 0      TMA producer (one lane): 4-stage ring of 48 KB (A 16 KB + B 32 KB)
+//   warp 1      TMEM allocator (all 512 columns) + single-thread tcgen05.mma
+//               issuer into two 256-column accumulators (double buffer)
+//   warps 2..9  epilogue: two warps per TMEM lane quadrant, each owning 128 of
+//               the 256 columns; rows go through a swizzled 4 KB shared-memory
+//               transpose per warp so every global store is a coalesced row
+//               write.  The epilogue of tile i overlaps the MMAs of tile i+1.
+// Epilogues fuse bias, RoPE, residual, RMSNorm (+ head gates of the next
+// transformer step), GELU, tanh, GLU and the complex mask application.
 // Every wait is time-bounded; a timeout sets the engine status word.
 #include <cstdio>
-#include <vector>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -20,14 +24,18 @@ namespace lbrr {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kBN = 256;
-constexpr int kStages = 2;
+constexpr int kStages = 4;
 constexpr int kABytes = kBM * kBK * 2;          // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;          // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
-constexpr int kBarOff = kStages * kStageBytes;
+constexpr int kEpiWarps = 8;
+constexpr int kStageWords = 32 * 32;            // per-warp transpose buffer (4 KB)
+constexpr int kStagingOff = kStages * kStageBytes;
+constexpr int kBarOff = kStagingOff + kEpiWarps * kStageWords * 4;
 constexpr int kGemmSmem = kBarOff + 256;
-constexpr int kGemmThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kGemmThreads = 64 + kEpiWarps * 32;
+constexpr uint32_t kTmemCols = 512;
+static_assert(kGemmSmem <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 
 // ---------------------------------------------------------------------------
 // Tile resolvers
@@ -53,10 +61,50 @@ struct TableTiles {
   __device__ TileDesc tile(int idx) const { return table[idx]; }
 };
 
+// Per-thread view handed to the epilogues.
+struct EpiCtx {
+  int lane, q, hsel;
+  int row;           // accumulator row (TMEM lane) 0..127
+  uint32_t tm;       // TMEM address of this warp's lanes in the current accumulator
+  uint32_t* stage;   // this warp's 32 x 32-word transpose buffer
+  uint32_t* peer;    // the buffer of the warp owning the other 128 columns of these rows
+  int bar_id;        // named barrier shared with that warp
+};
+
+__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
 // ---------------------------------------------------------------------------
+// Warp-cooperative row store through the transpose buffer: lane i holds W
+// 32-bit words of row i (W = 16: 32 fp16, W = 32: 32 fp32); afterwards each
+// store instruction writes whole 16-byte segments of consecutive rows.
+// row_ptr(r) returns the destination of row r or nullptr to skip it.
+// Swizzle (vector v of row r at v ^ s(r)) keeps both phases bank-conflict free.
+// ---------------------------------------------------------------------------
+template <int W, class RowPtr>
+__device__ __forceinline__ void warp_store_rows(uint32_t* stage, const uint32_t* w, int lane, RowPtr row_ptr) {
+  constexpr int V = W / 4;  // 16-byte vectors per row
+  const int sw = V == 8 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll
+  for (int k = 0; k < V; ++k)
+    *reinterpret_cast<uint4*>(stage + lane * W + ((k ^ sw) << 2)) =
+        make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  __syncwarp();
+  constexpr int RPI = 32 / V;  // rows per store instruction
+#pragma unroll
+  for (int it = 0; it < 32 / RPI; ++it) {
+    const int r = it * RPI + lane / V, v = lane % V;
+    const int s = V == 8 ? (r & 7) : ((r >> 1) & 3);
+    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * W + ((v ^ s) << 2));
+    char* p = row_ptr(r);
+    if (p) *reinterpret_cast<uint4*>(p + v * 16) = val;
+  }
+  __syncwarp();
+}
+
+__device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
 // GELU with the Abramowitz-Stegun 7.1.26 erf approximation (the published
 // formula the reference's FF1 epilogue uses, src/main.rs:2928-2935).
-// ---------------------------------------------------------------------------
 __device__ __forceinline__ float gelu_as(float v) {
   const float a = fabsf(v) * 0.70710678f;
   const float t = __fdividef(1.0f, 1.0f + 0.3275911f * a);
@@ -64,14 +112,6 @@ __device__ __forceinline__ float gelu_as(float v) {
                       0.254829592f) * t;
   const float erfa = copysignf(1.0f - poly * __expf(-a * a), v);
   return 0.5f * v * (1.0f + erfa);
-}
-
-__device__ __forceinline__ void store16w(void* dst, const uint32_t (&w)[16]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-  d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-  d[1] = make_uint4(w[4], w[5], w[6], w[7]);
-  d[2] = make_uint4(w[8], w[9], w[10], w[11]);
-  d[3] = make_uint4(w[12], w[13], w[14], w[15]);
 }
 
 // ---------------------------------------------------------------------------
@@ -87,92 +127,48 @@ struct EpiQKV : DenseTiles {
   const float* sin;
   __half* qkv;          // [M][1536]
   int nb, axis;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
-    const int pos = axis == 0 ? r / nb : r % nb;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+    const int r = t.row0 + x.row;
+    const bool valid = x.row < t.rows;
+    const int pos = valid ? (axis == 0 ? r / nb : r % nb) : 0;
+    const int rb = x.q * 32;
 #pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
+    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
       uint32_t v[32];
-      tmem_ld32(tm + c, v);
+      tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
-      if (!valid) continue;
       const int col = t.aux + c;
       const bool rot = col < 1024;
       const int pair0 = (col & 63) >> 1;
       uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float e = f16_round(__uint_as_float(v[2 * j]) + __ldg(bias16 + col + 2 * j));
-        float o = f16_round(__uint_as_float(v[2 * j + 1]) + __ldg(bias16 + col + 2 * j + 1));
+      for (int j4 = 0; j4 < 4; ++j4) {
+        const float4 b0 = ldg4(bias16 + col + 8 * j4), b1 = ldg4(bias16 + col + 8 * j4 + 4);
+        float4 cs = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
         if (rot) {
-          const float cs = __ldg(cos + pos * 32 + pair0 + j), sn = __ldg(sin + pos * 32 + pair0 + j);
-          const float e2 = __fsub_rn(__fmul_rn(e, cs), __fmul_rn(o, sn));
-          const float o2 = __fadd_rn(__fmul_rn(o, cs), __fmul_rn(e, sn));
-          e = e2;
-          o = o2;
+          cs = ldg4(cos + pos * 32 + pair0 + 4 * j4);
+          sn = ldg4(sin + pos * 32 + pair0 + 4 * j4);
         }
-        w[j] = pack_f16x2(e, o);
-      }
-      store16w(qkv + static_cast<size_t>(r) * 1536 + col, w);
-    }
-  }
-};
-
-// Out-projection: attn_out = acc + bias + x (fp32), then the pre-FF RMSNorm of
-// that row, (v*scale)*gamma rounded to fp16 (src/main.rs:6219-6234, :490-554).
-struct EpiOutNorm : DenseTiles {
-  const float* bias;   // [256]
-  const float* resid;  // x [M][256]
-  const float* gamma;  // [256]
-  float* out;          // attn_out [M][256]
-  __half* h16;         // [M][256]
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
-    float ss = 0.f;
-#pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(tm + c, v);
-      tmem_ld_wait(v);
-      if (valid) {
-        const float4* rs = reinterpret_cast<const float4*>(resid + static_cast<size_t>(r) * 256 + c);
-        float4* os = reinterpret_cast<float4*>(out + static_cast<size_t>(r) * 256 + c);
+        const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 x4 = rs[q];
-          float4 o;
-          o.x = __uint_as_float(v[4 * q + 0]) + __ldg(bias + c + 4 * q + 0) + x4.x;
-          o.y = __uint_as_float(v[4 * q + 1]) + __ldg(bias + c + 4 * q + 1) + x4.y;
-          o.z = __uint_as_float(v[4 * q + 2]) + __ldg(bias + c + 4 * q + 2) + x4.z;
-          o.w = __uint_as_float(v[4 * q + 3]) + __ldg(bias + c + 4 * q + 3) + x4.w;
-          os[q] = o;
-          ss += o.x * o.x + o.y * o.y + o.z * o.z + o.w * o.w;
-          v[4 * q + 0] = __float_as_uint(o.x);
-          v[4 * q + 1] = __float_as_uint(o.y);
-          v[4 * q + 2] = __float_as_uint(o.z);
-          v[4 * q + 3] = __float_as_uint(o.w);
+        for (int j = 0; j < 4; ++j) {
+          const int k = 8 * j4 + 2 * j;
+          float e = f16_round(__uint_as_float(v[k]) + bb[2 * j]);
+          float o = f16_round(__uint_as_float(v[k + 1]) + bb[2 * j + 1]);
+          if (rot) {
+            const float e2 = __fsub_rn(__fmul_rn(e, cc[j]), __fmul_rn(o, ss[j]));
+            const float o2 = __fadd_rn(__fmul_rn(o, cc[j]), __fmul_rn(e, ss[j]));
+            e = e2;
+            o = o2;
+          }
+          w[4 * j4 + j] = pack_f16x2(e, o);
         }
       }
-      tmem_st32(tm + c, v);
-    }
-    tmem_st_wait();
-    const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(tm + c, v);
-      tmem_ld_wait(v);
-      if (!valid) continue;
-      uint32_t w[16];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float a = __fmul_rn(__fmul_rn(__uint_as_float(v[2 * j]), scale), __ldg(gamma + c + 2 * j));
-        const float b = __fmul_rn(__fmul_rn(__uint_as_float(v[2 * j + 1]), scale), __ldg(gamma + c + 2 * j + 1));
-        w[j] = pack_f16x2(a, b);
-      }
-      store16w(h16 + static_cast<size_t>(r) * 256 + c, w);
+      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
+        return rb + rr < t.rows ? reinterpret_cast<char*>(qkv + static_cast<size_t>(t.row0 + rb + rr) * 1536 + col)
+                                : nullptr;
+      });
     }
   }
 };
@@ -182,88 +178,184 @@ struct EpiGelu : DenseTiles {
   const float* bias;  // [N]
   __half* out;        // [M][ldo]
   int ldo;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+    const int rb = x.q * 32;
 #pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
+    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
       uint32_t v[32];
-      tmem_ld32(tm + c, v);
+      tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
-      if (!valid) continue;
       const int col = t.aux + c;
       uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float a = gelu_as(__uint_as_float(v[2 * j]) + __ldg(bias + col + 2 * j));
-        const float b = gelu_as(__uint_as_float(v[2 * j + 1]) + __ldg(bias + col + 2 * j + 1));
-        w[j] = pack_f16x2(a, b);
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 b = ldg4(bias + col + 4 * j4);
+        w[2 * j4] = pack_f16x2(gelu_as(__uint_as_float(v[4 * j4]) + b.x), gelu_as(__uint_as_float(v[4 * j4 + 1]) + b.y));
+        w[2 * j4 + 1] =
+            pack_f16x2(gelu_as(__uint_as_float(v[4 * j4 + 2]) + b.z), gelu_as(__uint_as_float(v[4 * j4 + 3]) + b.w));
       }
-      store16w(out + static_cast<size_t>(r) * ldo + col, w);
+      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
+        return rb + rr < t.rows ? reinterpret_cast<char*>(out + static_cast<size_t>(t.row0 + rb + rr) * ldo + col)
+                                : nullptr;
+      });
     }
   }
 };
 
-// FF2: x = acc + b2 + attn_out (fp32) (src/main.rs:6255-6259).
+// Shared body of the N = 256 fp32-row epilogues: v = acc + bias (+ resid), v
+// stored as the fp32 output row, then an optional RMSNorm of the full row:
+//   norm == 1: pre-FF norm (v*scale)*gamma -> fp16            (rmsnorm_h16, src/main.rs:490-554)
+//   norm == 2: pre-attention norm v*(scale*gamma) -> fp16 plus
+//              the 8 head gates h.Wg + bg from the fp32 h     (rmsnorm_gates_h16, :616-703)
+//   norm == 3: final norm (v*scale)*gamma -> fp16, band-major (rmsnorm + transpose_band_major_h16,
+//                                                              :444-483, :1755-1770)
+// The two warps of a row quadrant exchange partial sums through their
+// transpose buffers under a 64-thread named barrier.
+struct RowNormParams {
+  int norm;             // 0 none, 1 pre-FF, 2 pre-attention + gates, 3 final
+  const float* gamma;   // [256]
+  const float* gate_w;  // [8][256]   (norm 2)
+  const float* gate_b;  // [8]        (norm 2)
+  __half* h16;          // [M][256]   (norm 1, 2)
+  float* gates;         // [M][8]     (norm 2)
+  __half* xb16;         // [nb][T][256] (norm 3)
+  int T, nb;            //            (norm 3)
+};
+
+template <class RowOf>
+__device__ __forceinline__ void row256_epilogue(const TileDesc& t, const EpiCtx& x, const float* bias,
+                                                const float* resid, float* out, const RowNormParams& np,
+                                                RowOf row_of) {
+  const bool valid = x.row < t.rows;
+  const int my_row = valid ? row_of(x.row) : 0;  // global token row of this thread
+  const int rb = x.q * 32;
+  const int c0 = x.hsel * 128;
+  float ss = 0.f;
+#pragma unroll 1
+  for (int c = c0; c < c0 + 128; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(x.tm + c, v);
+    tmem_ld_wait(v);
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 b = ldg4(bias + c + 4 * j4);
+      float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (resid && valid) rr = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(my_row) * 256 + c + 4 * j4);
+      const float o0 = __uint_as_float(v[4 * j4]) + b.x + rr.x;
+      const float o1 = __uint_as_float(v[4 * j4 + 1]) + b.y + rr.y;
+      const float o2 = __uint_as_float(v[4 * j4 + 2]) + b.z + rr.z;
+      const float o3 = __uint_as_float(v[4 * j4 + 3]) + b.w + rr.w;
+      ss += o0 * o0 + o1 * o1 + o2 * o2 + o3 * o3;
+      v[4 * j4] = __float_as_uint(o0);
+      v[4 * j4 + 1] = __float_as_uint(o1);
+      v[4 * j4 + 2] = __float_as_uint(o2);
+      v[4 * j4 + 3] = __float_as_uint(o3);
+    }
+    warp_store_rows<32>(x.stage, v, x.lane, [&](int r) -> char* {
+      return rb + r < t.rows ? reinterpret_cast<char*>(out + static_cast<size_t>(row_of(rb + r)) * 256 + c)
+                             : nullptr;
+    });
+    if (np.norm) tmem_st32(x.tm + c, v);
+  }
+  if (!np.norm) return;
+  tmem_st_wait();
+  // full-row sum of squares: exchange the two 128-column halves
+  x.stage[x.lane] = __float_as_uint(ss);
+  pair_sync(x.bar_id);
+  ss += __uint_as_float(x.peer[x.lane]);
+  pair_sync(x.bar_id);
+  const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
+  float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int c = c0; c < c0 + 128; c += 32) {
+    uint32_t v[32];
+    tmem_ld32(x.tm + c, v);
+    tmem_ld_wait(v);
+    uint32_t w[16];
+#pragma unroll
+    for (int j4 = 0; j4 < 8; ++j4) {
+      const float4 gm = ldg4(np.gamma + c + 4 * j4);
+      const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
+      float h[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float vv = __uint_as_float(v[4 * j4 + k]);
+        h[k] = np.norm == 2 ? __fmul_rn(vv, __fmul_rn(scale, gg[k])) : __fmul_rn(__fmul_rn(vv, scale), gg[k]);
+      }
+      if (np.norm == 2) {
+#pragma unroll
+        for (int gi = 0; gi < 8; ++gi) {
+          const float4 wg = ldg4(np.gate_w + gi * 256 + c + 4 * j4);
+          g[gi] += h[0] * wg.x + h[1] * wg.y + h[2] * wg.z + h[3] * wg.w;
+        }
+      }
+      w[2 * j4] = pack_f16x2(h[0], h[1]);
+      w[2 * j4 + 1] = pack_f16x2(h[2], h[3]);
+    }
+    if (np.norm == 3) {
+      warp_store_rows<16>(x.stage, w, x.lane, [&](int r) -> char* {
+        if (rb + r >= t.rows) return nullptr;
+        const int tok = row_of(rb + r), tt = tok / np.nb, bb = tok % np.nb;
+        return reinterpret_cast<char*>(np.xb16 + (static_cast<size_t>(bb) * np.T + tt) * 256 + c);
+      });
+    } else {
+      warp_store_rows<16>(x.stage, w, x.lane, [&](int r) -> char* {
+        return rb + r < t.rows ? reinterpret_cast<char*>(np.h16 + static_cast<size_t>(row_of(rb + r)) * 256 + c)
+                               : nullptr;
+      });
+    }
+  }
+  if (np.norm == 2) {
+#pragma unroll
+    for (int gi = 0; gi < 8; ++gi) x.stage[gi * 32 + x.lane] = __float_as_uint(g[gi]);
+    pair_sync(x.bar_id);
+    if (x.hsel == 0 && valid) {
+      float tot[8];
+#pragma unroll
+      for (int gi = 0; gi < 8; ++gi) tot[gi] = g[gi] + __uint_as_float(x.peer[gi * 32 + x.lane]) + __ldg(np.gate_b + gi);
+      float4* dst = reinterpret_cast<float4*>(np.gates + static_cast<size_t>(my_row) * 8);
+      dst[0] = make_float4(tot[0], tot[1], tot[2], tot[3]);
+      dst[1] = make_float4(tot[4], tot[5], tot[6], tot[7]);
+    }
+    pair_sync(x.bar_id);
+  }
+}
+
+// Out-projection: attn_out = acc + bias + x, fused with the pre-FF RMSNorm
+// (matmul_resid + rmsnorm_h16, src/main.rs:6219-6234).
+struct EpiOutNorm : DenseTiles {
+  const float* bias;
+  const float* resid;
+  float* out;
+  RowNormParams np;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+    row256_epilogue(t, x, bias, resid, out, np, [&](int r) { return t.row0 + r; });
+  }
+};
+
+// FF2: x = acc + b2 + attn_out (src/main.rs:6255-6259), fused with the next
+// step's pre-attention RMSNorm + gates, or after the last step with the final
+// norm in band-major fp16.
 struct EpiResid : DenseTiles {
   const float* bias;
   const float* resid;
   float* out;
-  int ldo;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
-#pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(tm + c, v);
-      tmem_ld_wait(v);
-      if (!valid) continue;
-      const int col = t.aux + c;
-      const float4* rs = reinterpret_cast<const float4*>(resid + static_cast<size_t>(r) * ldo + col);
-      float4* os = reinterpret_cast<float4*>(out + static_cast<size_t>(r) * ldo + col);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 x4 = rs[q];
-        float4 o;
-        o.x = __uint_as_float(v[4 * q + 0]) + __ldg(bias + col + 4 * q + 0) + x4.x;
-        o.y = __uint_as_float(v[4 * q + 1]) + __ldg(bias + col + 4 * q + 1) + x4.y;
-        o.z = __uint_as_float(v[4 * q + 2]) + __ldg(bias + col + 4 * q + 2) + x4.z;
-        o.w = __uint_as_float(v[4 * q + 3]) + __ldg(bias + col + 4 * q + 3) + x4.w;
-        os[q] = o;
-      }
-    }
+  RowNormParams np;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+    row256_epilogue(t, x, bias, resid, out, np, [&](int r) { return t.row0 + r; });
   }
 };
 
-// Band split: x[(t*nb + band)][n] = acc + bias[band][n]  (bandsplit_gemm_f16,
-// src/main.rs:4686-4698).  Tile aux = band.
+// Band split: x[(t*nb + band)][n] = acc + bias[band][n] (bandsplit_gemm_f16,
+// src/main.rs:4686-4698), fused with step 0's RMSNorm + gates.  Tile aux = band.
 struct EpiBand : TableTiles {
   const float* bias;  // [nb][256]
   float* x;           // [T*nb][256]
   int nb;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
+  RowNormParams np;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
     const int band = t.aux;
-#pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(tm + c, v);
-      tmem_ld_wait(v);
-      if (!valid) continue;
-      float4* os = reinterpret_cast<float4*>(x + (static_cast<size_t>(r) * nb + band) * 256 + c);
-      const float* bb = bias + band * 256 + c;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        float4 o;
-        o.x = __uint_as_float(v[4 * q + 0]) + __ldg(bb + 4 * q + 0);
-        o.y = __uint_as_float(v[4 * q + 1]) + __ldg(bb + 4 * q + 1);
-        o.z = __uint_as_float(v[4 * q + 2]) + __ldg(bb + 4 * q + 2);
-        o.w = __uint_as_float(v[4 * q + 3]) + __ldg(bb + 4 * q + 3);
-        os[q] = o;
-      }
-    }
+    row256_epilogue(t, x, bias + band * 256, nullptr, this->x, np, [&](int r) { return (t.row0 + r) * nb + band; });
   }
 };
 
@@ -273,25 +365,28 @@ struct EpiTanh : TableTiles {
   const float* bias;  // [groups][1024]
   __half* hidden;     // [groups*T][1024]
   int T;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
     const int group = t.aux >> 2, n0 = (t.aux & 3) * kBN;
+    const int rb = x.q * 32;
 #pragma unroll 1
-    for (int c = 0; c < kBN; c += 32) {
+    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
       uint32_t v[32];
-      tmem_ld32(tm + c, v);
+      tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
-      if (!valid) continue;
       const float* bb = bias + static_cast<size_t>(group) * 1024 + n0 + c;
       uint32_t w[16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float a = tanhf(__uint_as_float(v[2 * j]) + __ldg(bb + 2 * j));
-        const float b = tanhf(__uint_as_float(v[2 * j + 1]) + __ldg(bb + 2 * j + 1));
-        w[j] = pack_f16x2(a, b);
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 b = ldg4(bb + 4 * j4);
+        w[2 * j4] = pack_f16x2(tanhf(__uint_as_float(v[4 * j4]) + b.x), tanhf(__uint_as_float(v[4 * j4 + 1]) + b.y));
+        w[2 * j4 + 1] =
+            pack_f16x2(tanhf(__uint_as_float(v[4 * j4 + 2]) + b.z), tanhf(__uint_as_float(v[4 * j4 + 3]) + b.w));
       }
-      store16w(hidden + (static_cast<size_t>(group) * T + r) * 1024 + n0 + c, w);
+      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
+        return rb + rr < t.rows
+                   ? reinterpret_cast<char*>(hidden + (static_cast<size_t>(group) * T + t.row0 + rb + rr) * 1024 + n0 + c)
+                   : nullptr;
+      });
     }
   }
 };
@@ -310,21 +405,22 @@ struct EpiMask : TableTiles {
   const float2* spec;   // [2][T][1025]
   float2* out;          // [stems*2][T][1025]
   int T, n2tot;
-  __device__ void run(const TileDesc& t, int row, uint32_t tm) const {
-    const int r = t.row0 + row;
-    const bool valid = row < t.rows;
+  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+    const int r = t.row0 + x.row;
+    const bool valid = x.row < t.rows;
     const int stem = t.aux >> 16, band = (t.aux >> 8) & 255, n0 = (t.aux & 255) * kBN;
     const int d_b = band_d[band], f0 = band_f0[band];
     const float* bb = bias2 + static_cast<size_t>(stem) * n2tot + band_o2[band] + n0;
+    const int c_end = min(x.hsel * 128 + 128, t.n);
 #pragma unroll 1
-    for (int c = 0; c < t.n; c += 32) {
+    for (int c = x.hsel * 128; c < c_end; c += 32) {
       uint32_t v[32];
-      tmem_ld32(tm + c, v);
+      tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
       if (!valid) continue;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int lc = c + q * 8;      // column inside this tile
+        const int lc = c + q * 8;        // column inside this tile
         const int d0 = (n0 + lc) >> 1;  // first GLU index of this bin = fi*4
         if (lc < t.n && d0 < d_b) {
           float m[4];
@@ -354,32 +450,34 @@ struct EpiMask : TableTiles {
 };
 
 // ---------------------------------------------------------------------------
-// The kernel
+// The persistent kernel
 // ---------------------------------------------------------------------------
 template <class Epi>
-__global__ void __launch_bounds__(kGemmThreads, 2)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Epi epi,
-                   int* status) {
+                   int n_tiles, int* status) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
   uint64_t* empty = full + kStages;
-  uint64_t* acc_full = empty + kStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+  uint64_t* acc_full = empty + kStages;  // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if ((smem_u32(smem) & 1023u) != 0) {  // uniform across the CTA: nothing allocated yet
     if (threadIdx.x == 0) report_status(status, kDevSmemMisaligned);
     return;
   }
-  const TileDesc t = epi.tile(blockIdx.x);
-
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&acc_full[s], 1);
+      mbar_init(&acc_empty[s], kEpiWarps);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -397,41 +495,76 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- TMA producer ----------------
     if (lane == 0) {
-      for (int kb = 0; kb < t.kblocks; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, status)) break;
-        uint8_t* sa = smem + s * kStageBytes;
-        mbar_arrive_expect_tx(&full[s], kStageBytes);
-        tma_load_2d(sa, &tmA, &full[s], t.a_col + kb * kBK, t.a_row);
-        tma_load_2d(sa + kABytes, &tmB, &full[s], kb * kBK, t.b_row);
+      uint32_t kbg = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        const TileDesc t = epi.tile(tile);
+        for (int kb = 0; kb < t.kblocks; ++kb, ++kbg) {
+          const int s = kbg % kStages;
+          const uint32_t ph = (kbg / kStages) & 1;
+          if (!(ok = mbar_wait(&empty[s], ph ^ 1u, abort_flag, status))) break;
+          uint8_t* sa = smem + s * kStageBytes;
+          mbar_arrive_expect_tx(&full[s], kStageBytes);
+          tma_load_2d(sa, &tmA, &full[s], t.a_col + kb * kBK, t.a_row);
+          tma_load_2d(sa + kABytes, &tmB, &full[s], kb * kBK, t.b_row);
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(kBM, t.n);
-      for (int kb = 0; kb < t.kblocks; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t ph = (kb / kStages) & 1;
-        if (!mbar_wait(&full[s], ph, abort_flag, status)) break;
+      uint32_t kbg = 0;
+      bool ok = true;
+      int i = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++i) {
+        const TileDesc t = epi.tile(tile);
+        const int slot = i & 1;
+        if (!(ok = mbar_wait(&acc_empty[slot], ((i >> 1) & 1) ^ 1u, abort_flag, status))) break;
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + s * kStageBytes);
-        const uint32_t sb = sa + kABytes;
+        const uint32_t d = tmem + slot * kBN;
+        const uint32_t idesc = idesc_f16_f32(kBM, t.n);
+        for (int kb = 0; kb < t.kblocks; ++kb, ++kbg) {
+          const int s = kbg % kStages;
+          const uint32_t ph = (kbg / kStages) & 1;
+          if (!(ok = mbar_wait(&full[s], ph, abort_flag, status))) break;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * kStageBytes);
+          const uint32_t sb = sa + kABytes;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          mma_f16_ss(tmem, sdesc_sw128(sa + k * 32, 1024, 16), sdesc_sw128(sb + k * 32, 1024, 16), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_ss(d, sdesc_sw128(sa + k * 32, 1024, 16), sdesc_sw128(sb + k * 32, 1024, 16), idesc,
+                       (kb | k) != 0 ? 1u : 0u);
+          mma_commit(&empty[s]);
         }
-        mma_commit(&empty[s]);
+        mma_commit(&acc_full[slot]);
       }
-      mma_commit(acc_full);
     }
   } else {
-    const int q = warp & 3;  // the TMEM lane quadrant this warp may access
-    const bool ok = mbar_wait(acc_full, 0, abort_flag, status);
-    tc_fence_after();
-    if (ok && !*abort_flag) epi.run(t, q * 32 + lane, tmem + (static_cast<uint32_t>(q * 32) << 16));
+    // ---------------- epilogue warps ----------------
+    const int ew = warp - 2;  // 0..7
+    EpiCtx x;
+    x.lane = lane;
+    x.q = warp & 3;  // TMEM lane quadrant this warp may access
+    x.hsel = ew >> 2;
+    x.row = x.q * 32 + lane;
+    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStagingOff);
+    x.stage = staging + ew * kStageWords;
+    x.peer = staging + (ew ^ 4) * kStageWords;
+    x.bar_id = 1 + x.q;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
+      const TileDesc t = epi.tile(tile);
+      const int slot = i & 1;
+      if (!mbar_wait(&acc_full[slot], (i >> 1) & 1, abort_flag, status)) break;
+      tc_fence_after();
+      x.tm = tmem + (static_cast<uint32_t>(x.q * 32) << 16) + slot * kBN;
+      epi.run(t, x);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[slot]);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -444,6 +577,17 @@ __global__ void __launch_bounds__(kGemmThreads, 2)
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <class Epi>
 static cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const Epi& epi, int tiles, int* status,
                                cudaStream_t st) {
@@ -454,11 +598,32 @@ static cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const
     configured = true;
   }
   if (tiles <= 0) return cudaSuccess;
-  gemm_tc_kernel<Epi><<<tiles, kGemmThreads, kGemmSmem, st>>>(a, b, epi, status);
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  gemm_tc_kernel<Epi><<<grid, kGemmThreads, kGemmSmem, st>>>(a, b, epi, tiles, status);
   return cudaGetLastError();
 }
 
 static int dense_tiles(int M, int N) { return ((M + kBM - 1) / kBM) * (N / kBN); }
+
+static RowNormParams no_norm() {
+  RowNormParams p{};
+  p.norm = 0;
+  return p;
+}
+
+static RowNormParams to_params(const RowNorm& n) {
+  RowNormParams p{};
+  p.norm = n.kind;
+  p.gamma = n.gamma;
+  p.gate_w = n.gate_w;
+  p.gate_b = n.gate_b;
+  p.h16 = n.h16;
+  p.gates = n.gates;
+  p.xb16 = n.xb16;
+  p.T = n.T;
+  p.nb = n.nb;
+  return p;
+}
 
 cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, const float* cos, const float* sin,
                      __half* qkv, int M, int nb, int axis, int* status, cudaStream_t st) {
@@ -491,9 +656,11 @@ cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const flo
   ep.kblocks = 512 / kBK;
   ep.bias = bias;
   ep.resid = resid;
-  ep.gamma = gamma;
   ep.out = out;
-  ep.h16 = h16;
+  ep.np = no_norm();
+  ep.np.norm = 1;
+  ep.np.gamma = gamma;
+  ep.np.h16 = h16;
   return launch_gemm(ta, tb, ep, dense_tiles(M, 256), status, st);
 }
 
@@ -514,7 +681,7 @@ cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, 
 }
 
 cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2, const float* resid, float* x, int M,
-                           int* status, cudaStream_t st) {
+                           const RowNorm& next, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
   cudaError_t e = make_map_2d(&ta, ff1, 1024, M, 1024 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w2, 1024, 256, 1024 * 2, kBK, kBN);
@@ -526,30 +693,31 @@ cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2,
   ep.bias = b2;
   ep.resid = resid;
   ep.out = x;
-  ep.ldo = 256;
+  ep.np = to_params(next);
   return launch_gemm(ta, tb, ep, dense_tiles(M, 256), status, st);
 }
 
 cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, int wband_cols, const float* bias,
-                           float* x, int T, int nb, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st) {
+                           float* x, int T, int nb, const TileDesc* tiles, int n_tiles, const RowNorm& first,
+                           int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
   cudaError_t e = make_map_2d(&ta, xn, xn_cols, T, static_cast<uint64_t>(xn_cols) * 2, kBK, kBM);
-  if (e == cudaSuccess) e = make_map_2d(&tb, wband, wband_cols, static_cast<uint64_t>(nb) * 256,
-                                        static_cast<uint64_t>(wband_cols) * 2, kBK, kBN);
+  if (e == cudaSuccess)
+    e = make_map_2d(&tb, wband, wband_cols, static_cast<uint64_t>(nb) * 256, static_cast<uint64_t>(wband_cols) * 2,
+                    kBK, kBN);
   if (e != cudaSuccess) return e;
   EpiBand ep;
   ep.table = tiles;
   ep.bias = bias;
   ep.x = x;
   ep.nb = nb;
+  ep.np = to_params(first);
   return launch_gemm(ta, tb, ep, n_tiles, status, st);
 }
 
 cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __half* hidden, int T, int groups,
                        const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
-  const int nb_rows = groups;  // xb16 holds nb bands; w1 holds groups = stems*nb blocks
-  (void)nb_rows;
   cudaError_t e = make_map_2d(&ta, xb16, 256, static_cast<uint64_t>(T) * kNumBands, 256 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w1, 256, static_cast<uint64_t>(groups) * 1024, 256 * 2, kBK, kBN);
   if (e != cudaSuccess) return e;

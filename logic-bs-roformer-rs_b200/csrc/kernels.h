@@ -26,6 +26,20 @@ struct TileDesc {
   int n, row0, rows, aux;
 };
 
+// RMSNorm fused into an N = 256 fp32-row GEMM epilogue (out-projection, FF2,
+// band split): kind 0 none, 1 pre-FF norm -> h16, 2 pre-attention norm -> h16
+// plus the 8 head gates, 3 final norm -> band-major xb16.
+struct RowNorm {
+  int kind = 0;
+  const float* gamma = nullptr;
+  const float* gate_w = nullptr;
+  const float* gate_b = nullptr;
+  __half* h16 = nullptr;
+  float* gates = nullptr;
+  __half* xb16 = nullptr;
+  int T = 0, nb = 0;
+};
+
 // TMA tensor maps (fp16, 128-byte swizzle, zero OOB fill).
 cudaError_t make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
                         uint32_t box_inner, uint32_t box_outer);
@@ -40,9 +54,10 @@ cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const flo
 cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, __half* ff1, int M, int* status,
                           cudaStream_t st);
 cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2, const float* resid, float* x, int M,
-                           int* status, cudaStream_t st);
+                           const RowNorm& next, int* status, cudaStream_t st);
 cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, int wband_cols, const float* bias,
-                           float* x, int T, int nb, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
+                           float* x, int T, int nb, const TileDesc* tiles, int n_tiles, const RowNorm& first,
+                           int* status, cudaStream_t st);
 cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __half* hidden, int T, int groups,
                        const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
 cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, const int* band_f0,
@@ -60,7 +75,6 @@ cudaError_t band_norm(const float2* spec, const float* gamma, const int* band_ta
                       int nb, cudaStream_t st);
 cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, const float* gate_b, __half* h16,
                        float* gates, int rows, cudaStream_t st);
-cudaError_t final_norm_bandmajor(const float* x, const float* gamma, __half* xb16, int T, int nb, cudaStream_t st);
 cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_env, float* out, int len, int T,
                       int channels, cudaStream_t st);
 

@@ -1,7 +1,7 @@
 // Bandwidth-bound kernels of the chunk forward: STFT framing, band RMSNorm
-// (fused with the spectrum reorder), the pre-attention RMSNorm + head gates,
-// the final RMSNorm (band-major fp16 output) and the single-chunk ISTFT
-// overlap-add.  Also the TMA tensor-map helpers.
+// (fused with the spectrum reorder), the stand-alone pre-attention RMSNorm +
+// head gates (the forward fuses it into GEMM epilogues) and the single-chunk
+// ISTFT overlap-add.  Also the TMA tensor-map helpers.
 #include <mutex>
 
 #include "common.cuh"
@@ -192,37 +192,6 @@ cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, 
                        float* gates, int rows, cudaStream_t st) {
   const int warps = 16;
   norm_gates_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(x, gamma, gate_w, gate_b, h16, gates, rows);
-  return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
-// Final RMSNorm ((v*scale)*gamma, src/main.rs:444-483) written as fp16 in
-// band-major order xb16[b][t][256] (transpose_band_major_h16, :1755-1770).
-// ---------------------------------------------------------------------------
-__global__ void final_norm_kernel(const float* __restrict__ x, const float* __restrict__ gamma,
-                                  __half* __restrict__ xb16, int T, int nb) {
-  const int lane = threadIdx.x & 31;
-  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= static_cast<long long>(T) * nb) return;
-  const int t = static_cast<int>(row / nb), b = static_cast<int>(row % nb);
-  const float4* xr = reinterpret_cast<const float4*>(x + row * 256 + lane * 8);
-  const float4 p = xr[0], q = xr[1];
-  float v[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
-  float ss = 0.f;
-#pragma unroll
-  for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
-  ss = warp_sum(ss);
-  const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
-#pragma unroll
-  for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fmul_rn(v[k], scale), __ldg(gamma + lane * 8 + k));
-  uint4 packed = make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]), pack_f16x2(v[4], v[5]),
-                            pack_f16x2(v[6], v[7]));
-  reinterpret_cast<uint4*>(xb16 + (static_cast<long long>(b) * T + t) * 256)[lane] = packed;
-}
-
-cudaError_t final_norm_bandmajor(const float* x, const float* gamma, __half* xb16, int T, int nb, cudaStream_t st) {
-  const long long rows = static_cast<long long>(T) * nb;
-  final_norm_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(x, gamma, xb16, T, nb);
   return cudaGetLastError();
 }
 
