@@ -175,20 +175,39 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       if (!ok) break;
       tc_fence_after();
       const int key0 = j * 128;
-      auto key_ok = [&](int c) { return time_axis ? (key0 + c < T) : (c / nb == rseq); };
+      // valid keys of this row inside the tile: [lo, hi)
+      const int lo = time_axis ? 0 : rseq * nb;
+      const int hi = time_axis ? min(128, T - key0) : lo + nb;
+      const bool full = lo == 0 && hi >= 128;  // warp-uniform on the time axis
       float mx = -INFINITY;
 #pragma unroll 1
       for (int c = 0; c < 128; c += 32) {
         uint32_t v[32];
         tmem_ld32(tS + c, v);
         tmem_ld_wait(v);
+        if (full) {
 #pragma unroll
-        for (int k = 0; k < 32; ++k)
-          if (key_ok(c + k)) mx = fmaxf(mx, __uint_as_float(v[k]));
+          for (int k = 0; k < 32; ++k) mx = fmaxf(mx, __uint_as_float(v[k]));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (c + k >= lo && c + k < hi) mx = fmaxf(mx, __uint_as_float(v[k]));
+        }
       }
       const float m_new = fmaxf(m_run, mx);
-      const float m_use = m_new == -INFINITY ? 0.f : m_new;
-      const float corr = ex2((m_run - m_use) * sc);
+      // Keep the running reference max unless the row max grew by more than
+      // 2^8 in exp2 units: exponents stay <= 2^8 (exact enough in fp32 and in
+      // the fp16 P), and O needs no rescale on most tiles.
+      float m_use, corr, m_next;
+      if (m_run == -INFINITY || (m_new - m_run) * sc > 8.0f) {
+        m_use = m_new == -INFINITY ? 0.f : m_new;
+        corr = ex2((m_run - m_use) * sc);
+        m_next = m_new;
+      } else {
+        m_use = m_run;
+        corr = 1.0f;
+        m_next = m_run;
+      }
       const float msc = m_use * sc;
       if (j > 0) {
         // PV_{j-1} must be done before O is rescaled and P is overwritten
@@ -215,12 +234,23 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         tmem_ld32(tS + c, v);
         tmem_ld_wait(v);
         uint32_t w[16];
+        if (full) {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float p0 = key_ok(c + 2 * k) ? ex2(__uint_as_float(v[2 * k]) * sc - msc) : 0.f;
-          const float p1 = key_ok(c + 2 * k + 1) ? ex2(__uint_as_float(v[2 * k + 1]) * sc - msc) : 0.f;
-          sum += p0 + p1;
-          w[k] = pack_f16x2(p0, p1);
+          for (int k = 0; k < 16; ++k) {
+            const float p0 = ex2(__uint_as_float(v[2 * k]) * sc - msc);
+            const float p1 = ex2(__uint_as_float(v[2 * k + 1]) * sc - msc);
+            sum += p0 + p1;
+            w[k] = pack_f16x2(p0, p1);
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const int c0 = c + 2 * k;
+            const float p0 = (c0 >= lo && c0 < hi) ? ex2(__uint_as_float(v[2 * k]) * sc - msc) : 0.f;
+            const float p1 = (c0 + 1 >= lo && c0 + 1 < hi) ? ex2(__uint_as_float(v[2 * k + 1]) * sc - msc) : 0.f;
+            sum += p0 + p1;
+            w[k] = pack_f16x2(p0, p1);
+          }
         }
         // row r of the K-major [128 rows][128 keys] P operand: key block c/64,
         // 16-byte chunk ((c%64)/8 + i) swizzled with (r & 7)
@@ -233,7 +263,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         }
       }
       l_run = l_run * corr + sum;
-      m_run = m_new;
+      m_run = m_next;
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);

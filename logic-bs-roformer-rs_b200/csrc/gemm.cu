@@ -3,14 +3,16 @@
 // One persistent kernel template computes, for every 128 x n output tile,
 // D = A[128 x K] * B[n x K]^T with fp16 operands (both K-major, 128-byte
 // swizzled, fed by TMA) and an fp32 accumulator in TMEM.  One CTA per SM
-// walks the tile list with a static stride.  Warp roles (320 threads):
+// walks the tile list with a static stride.  Warp roles (64 + 32 * kEpiWarps threads):
 //   warp 0      TMA producer (one lane): 4-stage ring of 48 KB (A 16 KB + B 32 KB)
 //   warp 1      TMEM allocator (all 512 columns) + single-thread tcgen05.mma
 //               issuer into two 256-column accumulators (double buffer)
 //   warps 2..9  epilogue: two warps per TMEM lane quadrant, each owning 128 of
-//               the 256 columns; rows go through a swizzled 4 KB shared-memory
-//               transpose per warp so every global store is a coalesced row
-//               write.  The epilogue of tile i overlaps the MMAs of tile i+1.
+//               the 256 columns, one accumulator row per thread.  Each 32 x 32
+//               output block is written into a 4 KB per-warp staging buffer in
+//               the TMA swizzle layout and leaves through a TMA tensor store, so
+//               the LSU carries neither the transpose read-back nor the global
+//               stores.  The epilogue of tile i overlaps the MMAs of tile i+1.
 // Epilogues fuse bias, RoPE, residual, RMSNorm (+ head gates of the next
 // transformer step), GELU, tanh, GLU and the complex mask application.
 // Every wait is time-bounded; a timeout sets the engine status word.
@@ -29,7 +31,9 @@ constexpr int kABytes = kBM * kBK * 2;          // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;          // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
 constexpr int kEpiWarps = 8;
-constexpr int kStageWords = 32 * 32;            // per-warp transpose buffer (4 KB)
+constexpr int kParts = kEpiWarps / 4;           // epilogue warps per TMEM lane quadrant
+constexpr int kPartCols = kBN / kParts;         // accumulator columns per epilogue warp
+constexpr int kStageWords = 32 * 32;            // per-warp staging buffer (4 KB)
 constexpr int kStagingOff = kStages * kStageBytes;
 constexpr int kBarOff = kStagingOff + kEpiWarps * kStageWords * 4;
 constexpr int kGemmSmem = kBarOff + 256;
@@ -61,57 +65,169 @@ struct TableTiles {
   __device__ TileDesc tile(int idx) const { return table[idx]; }
 };
 
-// Per-thread view handed to the epilogues.
-struct EpiCtx {
-  int lane, q, hsel;
-  int row;           // accumulator row (TMEM lane) 0..127
-  uint32_t tm;       // TMEM address of this warp's lanes in the current accumulator
-  uint32_t* stage;   // this warp's 32 x 32-word transpose buffer
-  uint32_t* peer;    // the buffer of the warp owning the other 128 columns of these rows
-  int bar_id;        // named barrier shared with that warp
+// ---------------------------------------------------------------------------
+// Per-warp staging buffer.  fp16 blocks (32 x 32 halves = 2 KB) alternate
+// between the two 1024-aligned halves so a TMA store can drain one while the
+// next block is written; fp32 blocks (4 KB) use the whole buffer.  Rows are
+// stored with the TMA swizzle of their width (64 B rows: 16-byte vector v of
+// row r at v ^ ((r >> 1) & 3); 128 B rows: v ^ (r & 7)), which also keeps the
+// per-lane row writes free of bank conflicts.
+// ---------------------------------------------------------------------------
+struct Stager {
+  uint32_t* base;
+  int lane;
+  int phase;
+  bool last_f32;
+  __device__ uint32_t* f16_buf() {
+    if (lane == 0) {
+      if (last_f32)
+        tma_store_wait_read<0>();
+      else
+        tma_store_wait_read<1>();
+    }
+    __syncwarp();
+    last_f32 = false;
+    return base + ((phase++) & 1) * 512;
+  }
+  __device__ uint32_t* f32_buf() {
+    if (lane == 0) tma_store_wait_read<0>();
+    __syncwarp();
+    last_f32 = true;
+    return base;
+  }
+  __device__ void drain() {
+    if (lane == 0) tma_store_wait_read<0>();
+    __syncwarp();
+  }
 };
 
-__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+// Per-thread view handed to the epilogues.
+struct EpiCtx {
+  int lane, q, part;
+  int c0;           // first accumulator column of this warp (part * kPartCols)
+  int row;          // accumulator row (TMEM lane) 0..127
+  uint32_t tm;      // TMEM address of this warp's lanes in the current accumulator
+  Stager st;        // this warp's staging buffer
+  uint32_t* quad;   // staging buffers of the kParts warps sharing these rows (part-major)
+  int bar_id;       // named barrier shared by those warps
+};
 
-// ---------------------------------------------------------------------------
-// Warp-cooperative row store through the transpose buffer: lane i holds W
-// 32-bit words of row i (W = 16: 32 fp16, W = 32: 32 fp32); afterwards each
-// store instruction writes whole 16-byte segments of consecutive rows.
-// row_ptr(r) returns the destination of row r or nullptr to skip it.
-// Swizzle (vector v of row r at v ^ s(r)) keeps both phases bank-conflict free.
-// ---------------------------------------------------------------------------
-template <int W, class RowPtr>
-__device__ __forceinline__ void warp_store_rows(uint32_t* stage, const uint32_t* w, int lane, RowPtr row_ptr) {
-  constexpr int V = W / 4;  // 16-byte vectors per row
+// Write this lane's row (W = 16 words: 32 fp16, W = 32: 32 fp32) into buf.
+template <int W>
+__device__ __forceinline__ void stage_row(uint32_t* buf, const uint32_t* w, int lane) {
+  constexpr int V = W / 4;
   const int sw = V == 8 ? (lane & 7) : ((lane >> 1) & 3);
 #pragma unroll
   for (int k = 0; k < V; ++k)
-    *reinterpret_cast<uint4*>(stage + lane * W + ((k ^ sw) << 2)) =
+    *reinterpret_cast<uint4*>(buf + lane * W + ((k ^ sw) << 2)) =
         make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+}
+// Publish the staged block to the async proxy; lane 0 then issues the store.
+__device__ __forceinline__ bool stage_publish(int lane) {
+  fence_proxy_async_smem();
   __syncwarp();
-  constexpr int RPI = 32 / V;  // rows per store instruction
+  return lane == 0;
+}
+__device__ __forceinline__ void store_2d(const CUtensorMap* m, const uint32_t* buf, int x, int y, int lane) {
+  if (stage_publish(lane)) {
+    tma_store_2d(m, buf, x, y);
+    tma_store_commit();
+  }
+}
+__device__ __forceinline__ void store_3d(const CUtensorMap* m, const uint32_t* buf, int x, int y, int z, int lane) {
+  if (stage_publish(lane)) {
+    tma_store_3d(m, buf, x, y, z);
+    tma_store_commit();
+  }
+}
+// Manual store of a staged fp16 block (rows with scattered destinations).
+template <class RowPtr>
+__device__ __forceinline__ void store_rows16_manual(const uint32_t* buf, int lane, RowPtr row_ptr) {
+  __syncwarp();
 #pragma unroll
-  for (int it = 0; it < 32 / RPI; ++it) {
-    const int r = it * RPI + lane / V, v = lane % V;
-    const int s = V == 8 ? (r & 7) : ((r >> 1) & 3);
-    const uint4 val = *reinterpret_cast<const uint4*>(stage + r * W + ((v ^ s) << 2));
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + lane / 4, v = lane % 4;
+    const uint4 val = *reinterpret_cast<const uint4*>(buf + r * 16 + ((v ^ ((r >> 1) & 3)) << 2));
     char* p = row_ptr(r);
     if (p) *reinterpret_cast<uint4*>(p + v * 16) = val;
   }
   __syncwarp();
 }
+// Coalesced load of a 32 x 32 fp32 block (rows rb.., columns c..) through the
+// staging buffer; lane i receives row i.  Rows >= rows_valid read as zero.
+__device__ __forceinline__ void load_rows32(uint32_t* buf, const float* src, size_t ld, int rows_valid, int lane,
+                                            uint32_t (&out)[32]) {
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + lane / 8, v = lane % 8;
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows_valid) val = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(r) * ld + v * 4);
+    *reinterpret_cast<uint4*>(buf + r * 32 + ((v ^ (r & 7)) << 2)) = val;
+  }
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 val = *reinterpret_cast<const uint4*>(buf + lane * 32 + ((k ^ (lane & 7)) << 2));
+    out[4 * k] = val.x;
+    out[4 * k + 1] = val.y;
+    out[4 * k + 2] = val.z;
+    out[4 * k + 3] = val.w;
+  }
+  __syncwarp();
+}
+
+// Barrier over the kParts warps that own the same 32 accumulator rows.
+__device__ __forceinline__ void quad_sync(int id) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kParts * 32) : "memory");
+}
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
 
-// GELU with the Abramowitz-Stegun 7.1.26 erf approximation (the published
-// formula the reference's FF1 epilogue uses, src/main.rs:2928-2935).
-__device__ __forceinline__ float gelu_as(float v) {
-  const float a = fabsf(v) * 0.70710678f;
-  const float t = __fdividef(1.0f, 1.0f + 0.3275911f * a);
-  const float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
-                      0.254829592f) * t;
-  const float erfa = copysignf(1.0f - poly * __expf(-a * a), v);
-  return 0.5f * v * (1.0f + erfa);
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+
+// GELU of two values with the Abramowitz-Stegun 7.1.26 erf approximation (the
+// published formula the reference's FF1 epilogue uses, src/main.rs:2928-2935),
+// written with packed fp32x2 FMA/MUL/ADD (same IEEE result per element as the
+// scalar ops, half the instructions).
+__device__ __forceinline__ float2 gelu_as2(float2 v) {
+  const float2 a = __fmul2_rn(f2(fabsf(v.x), fabsf(v.y)), f2(0.70710678f, 0.70710678f));
+  const float2 den = __ffma2_rn(a, f2(0.3275911f, 0.3275911f), f2(1.0f, 1.0f));
+  const float2 t = f2(rcp_approx(den.x), rcp_approx(den.y));
+  float2 p = __ffma2_rn(f2(1.061405429f, 1.061405429f), t, f2(-1.453152027f, -1.453152027f));
+  p = __ffma2_rn(p, t, f2(1.421413741f, 1.421413741f));
+  p = __ffma2_rn(p, t, f2(-0.284496736f, -0.284496736f));
+  p = __ffma2_rn(p, t, f2(0.254829592f, 0.254829592f));
+  p = __fmul2_rn(p, t);
+  // exp(-a^2) = 2^(-a^2 * log2 e)
+  const float2 arg = __fmul2_rn(__fmul2_rn(a, a), f2(-1.4426950408889634f, -1.4426950408889634f));
+  const float2 e = f2(ex2_approx(arg.x), ex2_approx(arg.y));
+  const float2 erfc = __fmul2_rn(p, e);
+  const float2 erfa = f2(copysignf(1.0f - erfc.x, v.x), copysignf(1.0f - erfc.y, v.y));
+  const float2 h = __fmul2_rn(v, f2(0.5f, 0.5f));
+  return __ffma2_rn(h, erfa, h);  // 0.5 v (1 + erf)
+}
+
+// tanh accurate to ~1e-6 relative (far below the fp16 rounding of the
+// mask estimator's hidden layer): odd Taylor series x(1 - x^2/3 + 2x^4/15)
+// for |x| < 1/16 (truncation < 4e-10), else (1 - e)/(1 + e) with
+// e = exp(-2|x|) from ex2, sign restored.
+__device__ __forceinline__ float tanh_fast(float x) {
+  const float ax = fabsf(x);
+  const float e = ex2_approx(ax * -2.8853900817779268f);  // -2 log2(e)
+  const float big = (1.0f - e) * rcp_approx(1.0f + e);
+  const float x2 = x * x;
+  const float small = ax * fmaf(x2, fmaf(x2, 0.13333333f, -0.33333333f), 1.0f);
+  return copysignf(ax < 0.0625f ? small : big, x);
 }
 
 // ---------------------------------------------------------------------------
@@ -122,18 +238,17 @@ __device__ __forceinline__ float gelu_as(float v) {
 // and rounded again -- the rounding points of cuBLASLt f16-out QKV followed by
 // rope_q16_inplace / rope_k16 (src/main.rs:6157-6187, :3684-3754).
 struct EpiQKV : DenseTiles {
+  CUtensorMap out_map;  // qkv [M][1536] fp16, box 32 x 32, 64-byte swizzle
   const float* bias16;  // [1536], values already rounded to fp16
   const float* cos;     // [P][32]
   const float* sin;
-  __half* qkv;          // [M][1536]
   int nb, axis;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int r = t.row0 + x.row;
     const bool valid = x.row < t.rows;
     const int pos = valid ? (axis == 0 ? r / nb : r % nb) : 0;
-    const int rb = x.q * 32;
 #pragma unroll 1
-    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
+    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
       uint32_t v[32];
       tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
@@ -154,34 +269,35 @@ struct EpiQKV : DenseTiles {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int k = 8 * j4 + 2 * j;
-          float e = f16_round(__uint_as_float(v[k]) + bb[2 * j]);
-          float o = f16_round(__uint_as_float(v[k + 1]) + bb[2 * j + 1]);
+          const float2 eo = __fadd2_rn(f2(__uint_as_float(v[k]), __uint_as_float(v[k + 1])), f2(bb[2 * j], bb[2 * j + 1]));
+          const uint32_t q16 = pack_f16x2(eo.x, eo.y);
           if (rot) {
-            const float e2 = __fsub_rn(__fmul_rn(e, cc[j]), __fmul_rn(o, ss[j]));
-            const float o2 = __fadd_rn(__fmul_rn(o, cc[j]), __fmul_rn(e, ss[j]));
-            e = e2;
-            o = o2;
+            // (e c - o s, o c + e s) from the fp16-rounded pair, products rounded
+            // separately like the reference's rope kernels
+            const float2 r = unpack_f16x2(q16);
+            const float2 p1 = __fmul2_rn(r, f2(cc[j], cc[j]));
+            const float2 p2 = __fmul2_rn(f2(r.y, r.x), f2(-ss[j], ss[j]));
+            const float2 o2 = __fadd2_rn(p1, p2);
+            w[4 * j4 + j] = pack_f16x2(o2.x, o2.y);
+          } else {
+            w[4 * j4 + j] = q16;
           }
-          w[4 * j4 + j] = pack_f16x2(e, o);
         }
       }
-      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
-        return rb + rr < t.rows ? reinterpret_cast<char*>(qkv + static_cast<size_t>(t.row0 + rb + rr) * 1536 + col)
-                                : nullptr;
-      });
+      uint32_t* buf = x.st.f16_buf();
+      stage_row<16>(buf, w, x.lane);
+      store_2d(&out_map, buf, col, t.row0 + x.q * 32, x.lane);
     }
   }
 };
 
 // FF1: f16(gelu_AS(acc + b1)) (gemm_f16_gelu_a16w epilogue, src/main.rs:2918-2948).
 struct EpiGelu : DenseTiles {
-  const float* bias;  // [N]
-  __half* out;        // [M][ldo]
-  int ldo;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
-    const int rb = x.q * 32;
+  CUtensorMap out_map;  // ff1 [M][1024] fp16, box 32 x 32, 64-byte swizzle
+  const float* bias;    // [N]
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
 #pragma unroll 1
-    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
+    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
       uint32_t v[32];
       tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
@@ -190,14 +306,15 @@ struct EpiGelu : DenseTiles {
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const float4 b = ldg4(bias + col + 4 * j4);
-        w[2 * j4] = pack_f16x2(gelu_as(__uint_as_float(v[4 * j4]) + b.x), gelu_as(__uint_as_float(v[4 * j4 + 1]) + b.y));
-        w[2 * j4 + 1] =
-            pack_f16x2(gelu_as(__uint_as_float(v[4 * j4 + 2]) + b.z), gelu_as(__uint_as_float(v[4 * j4 + 3]) + b.w));
+        const float2 g0 = gelu_as2(__fadd2_rn(f2(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1])), f2(b.x, b.y)));
+        const float2 g1 =
+            gelu_as2(__fadd2_rn(f2(__uint_as_float(v[4 * j4 + 2]), __uint_as_float(v[4 * j4 + 3])), f2(b.z, b.w)));
+        w[2 * j4] = pack_f16x2(g0.x, g0.y);
+        w[2 * j4 + 1] = pack_f16x2(g1.x, g1.y);
       }
-      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
-        return rb + rr < t.rows ? reinterpret_cast<char*>(out + static_cast<size_t>(t.row0 + rb + rr) * ldo + col)
-                                : nullptr;
-      });
+      uint32_t* buf = x.st.f16_buf();
+      stage_row<16>(buf, w, x.lane);
+      store_2d(&out_map, buf, col, t.row0 + x.q * 32, x.lane);
     }
   }
 };
@@ -209,65 +326,91 @@ struct EpiGelu : DenseTiles {
 //              the 8 head gates h.Wg + bg from the fp32 h     (rmsnorm_gates_h16, :616-703)
 //   norm == 3: final norm (v*scale)*gamma -> fp16, band-major (rmsnorm + transpose_band_major_h16,
 //                                                              :444-483, :1755-1770)
-// The two warps of a row quadrant exchange partial sums through their
-// transpose buffers under a 64-thread named barrier.
+// The warps of a row quadrant exchange partial sums through their staging
+// buffers under a named barrier.  Dense rows use 2-D store maps; the band
+// split's rows (t*nb + band) use 3-D maps over [T][nb][256].
 struct RowNormParams {
   int norm;             // 0 none, 1 pre-FF, 2 pre-attention + gates, 3 final
   const float* gamma;   // [256]
   const float* gate_w;  // [8][256]   (norm 2)
   const float* gate_b;  // [8]        (norm 2)
-  __half* h16;          // [M][256]   (norm 1, 2)
   float* gates;         // [M][8]     (norm 2)
   __half* xb16;         // [nb][T][256] (norm 3)
   int T, nb;            //            (norm 3)
 };
 
-template <class RowOf>
-__device__ __forceinline__ void row256_epilogue(const TileDesc& t, const EpiCtx& x, const float* bias,
-                                                const float* resid, float* out, const RowNormParams& np,
+struct Row256Maps {
+  CUtensorMap out_map;  // fp32 rows, box 32 x 32 (2-D) or 32 x 1 x 32 (3-D), 128-byte swizzle
+  CUtensorMap h16_map;  // fp16 rows (norm 1, 2), box 32 x 32 (x 1), 64-byte swizzle
+};
+
+template <bool kBandRows, class RowOf>
+__device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, const float* bias, const float* resid,
+                                                const Row256Maps& maps, const RowNormParams& np, int band,
                                                 RowOf row_of) {
   const bool valid = x.row < t.rows;
   const int my_row = valid ? row_of(x.row) : 0;  // global token row of this thread
   const int rb = x.q * 32;
-  const int c0 = x.hsel * 128;
+  const int rows_valid = min(32, t.rows - rb);
+  const int c0 = x.c0;
+  auto store_out = [&](const CUtensorMap* m, const uint32_t* buf, int c) {
+    if (kBandRows)
+      store_3d(m, buf, c, band, t.row0 + rb, x.lane);
+    else
+      store_2d(m, buf, c, t.row0 + rb, x.lane);
+  };
+  (void)rows_valid;
+  // this thread's residual row, 32 columns at a time, loaded one chunk ahead
+  const float* rrow = (resid && valid) ? resid + static_cast<size_t>(my_row) * 256 : nullptr;
+  float4 rr[8], rn[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) rr[k] = rrow ? *reinterpret_cast<const float4*>(rrow + c0 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
   float ss = 0.f;
 #pragma unroll 1
-  for (int c = c0; c < c0 + 128; c += 32) {
+  for (int c = c0; c < c0 + kPartCols; c += 32) {
+    const bool more = c + 32 < c0 + kPartCols;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      rn[k] = (rrow && more) ? *reinterpret_cast<const float4*>(rrow + c + 32 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t v[32];
     tmem_ld32(x.tm + c, v);
     tmem_ld_wait(v);
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
       const float4 b = ldg4(bias + c + 4 * j4);
-      float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (resid && valid) rr = *reinterpret_cast<const float4*>(resid + static_cast<size_t>(my_row) * 256 + c + 4 * j4);
-      const float o0 = __uint_as_float(v[4 * j4]) + b.x + rr.x;
-      const float o1 = __uint_as_float(v[4 * j4 + 1]) + b.y + rr.y;
-      const float o2 = __uint_as_float(v[4 * j4 + 2]) + b.z + rr.z;
-      const float o3 = __uint_as_float(v[4 * j4 + 3]) + b.w + rr.w;
-      ss += o0 * o0 + o1 * o1 + o2 * o2 + o3 * o3;
-      v[4 * j4] = __float_as_uint(o0);
-      v[4 * j4 + 1] = __float_as_uint(o1);
-      v[4 * j4 + 2] = __float_as_uint(o2);
-      v[4 * j4 + 3] = __float_as_uint(o3);
+      const float2 o01 = __fadd2_rn(__fadd2_rn(f2(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1])), f2(b.x, b.y)),
+                                    f2(rr[j4].x, rr[j4].y));
+      const float2 o23 =
+          __fadd2_rn(__fadd2_rn(f2(__uint_as_float(v[4 * j4 + 2]), __uint_as_float(v[4 * j4 + 3])), f2(b.z, b.w)),
+                     f2(rr[j4].z, rr[j4].w));
+      const float2 sq = __ffma2_rn(o01, o01, __fmul2_rn(o23, o23));
+      ss += sq.x + sq.y;
+      v[4 * j4] = __float_as_uint(o01.x);
+      v[4 * j4 + 1] = __float_as_uint(o01.y);
+      v[4 * j4 + 2] = __float_as_uint(o23.x);
+      v[4 * j4 + 3] = __float_as_uint(o23.y);
     }
-    warp_store_rows<32>(x.stage, v, x.lane, [&](int r) -> char* {
-      return rb + r < t.rows ? reinterpret_cast<char*>(out + static_cast<size_t>(row_of(rb + r)) * 256 + c)
-                             : nullptr;
-    });
+#pragma unroll
+    for (int k = 0; k < 8; ++k) rr[k] = rn[k];
+    uint32_t* buf = x.st.f32_buf();
+    stage_row<32>(buf, v, x.lane);
+    store_out(&maps.out_map, buf, c);
     if (np.norm) tmem_st32(x.tm + c, v);
   }
   if (!np.norm) return;
   tmem_st_wait();
-  // full-row sum of squares: exchange the two 128-column halves
-  x.stage[x.lane] = __float_as_uint(ss);
-  pair_sync(x.bar_id);
-  ss += __uint_as_float(x.peer[x.lane]);
-  pair_sync(x.bar_id);
+  // full-row sum of squares over the warps sharing these rows
+  x.st.drain();
+  x.st.base[x.lane] = __float_as_uint(ss);
+  quad_sync(x.bar_id);
+  ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < kParts; ++p) ss += __uint_as_float(x.quad[p * kStageWords + x.lane]);
+  quad_sync(x.bar_id);
   const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
   float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-  for (int c = c0; c < c0 + 128; c += 32) {
+  for (int c = c0; c < c0 + kPartCols; c += 32) {
     uint32_t v[32];
     tmem_ld32(x.tm + c, v);
     tmem_ld_wait(v);
@@ -292,84 +435,77 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, const EpiCtx&
       w[2 * j4] = pack_f16x2(h[0], h[1]);
       w[2 * j4 + 1] = pack_f16x2(h[2], h[3]);
     }
+    uint32_t* buf = x.st.f16_buf();
+    stage_row<16>(buf, w, x.lane);
     if (np.norm == 3) {
-      warp_store_rows<16>(x.stage, w, x.lane, [&](int r) -> char* {
+      store_rows16_manual(buf, x.lane, [&](int r) -> char* {
         if (rb + r >= t.rows) return nullptr;
         const int tok = row_of(rb + r), tt = tok / np.nb, bb = tok % np.nb;
         return reinterpret_cast<char*>(np.xb16 + (static_cast<size_t>(bb) * np.T + tt) * 256 + c);
       });
     } else {
-      warp_store_rows<16>(x.stage, w, x.lane, [&](int r) -> char* {
-        return rb + r < t.rows ? reinterpret_cast<char*>(np.h16 + static_cast<size_t>(row_of(rb + r)) * 256 + c)
-                               : nullptr;
-      });
+      store_out(&maps.h16_map, buf, c);
     }
   }
   if (np.norm == 2) {
+    x.st.drain();
 #pragma unroll
-    for (int gi = 0; gi < 8; ++gi) x.stage[gi * 32 + x.lane] = __float_as_uint(g[gi]);
-    pair_sync(x.bar_id);
-    if (x.hsel == 0 && valid) {
+    for (int gi = 0; gi < 8; ++gi) x.st.base[gi * 32 + x.lane] = __float_as_uint(g[gi]);
+    quad_sync(x.bar_id);
+    if (x.part == 0 && valid) {
       float tot[8];
 #pragma unroll
-      for (int gi = 0; gi < 8; ++gi) tot[gi] = g[gi] + __uint_as_float(x.peer[gi * 32 + x.lane]) + __ldg(np.gate_b + gi);
+      for (int gi = 0; gi < 8; ++gi) {
+        tot[gi] = __ldg(np.gate_b + gi);
+#pragma unroll
+        for (int p = 0; p < kParts; ++p) tot[gi] += __uint_as_float(x.quad[p * kStageWords + gi * 32 + x.lane]);
+      }
       float4* dst = reinterpret_cast<float4*>(np.gates + static_cast<size_t>(my_row) * 8);
       dst[0] = make_float4(tot[0], tot[1], tot[2], tot[3]);
       dst[1] = make_float4(tot[4], tot[5], tot[6], tot[7]);
     }
-    pair_sync(x.bar_id);
+    quad_sync(x.bar_id);
   }
 }
 
 // Out-projection: attn_out = acc + bias + x, fused with the pre-FF RMSNorm
 // (matmul_resid + rmsnorm_h16, src/main.rs:6219-6234).
-struct EpiOutNorm : DenseTiles {
-  const float* bias;
-  const float* resid;
-  float* out;
-  RowNormParams np;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
-    row256_epilogue(t, x, bias, resid, out, np, [&](int r) { return t.row0 + r; });
-  }
-};
-
 // FF2: x = acc + b2 + attn_out (src/main.rs:6255-6259), fused with the next
 // step's pre-attention RMSNorm + gates, or after the last step with the final
 // norm in band-major fp16.
-struct EpiResid : DenseTiles {
+struct EpiRow256 : DenseTiles {
+  Row256Maps maps;
   const float* bias;
   const float* resid;
-  float* out;
   RowNormParams np;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
-    row256_epilogue(t, x, bias, resid, out, np, [&](int r) { return t.row0 + r; });
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
+    row256_epilogue<false>(t, x, bias, resid, maps, np, 0, [&](int r) { return t.row0 + r; });
   }
 };
 
 // Band split: x[(t*nb + band)][n] = acc + bias[band][n] (bandsplit_gemm_f16,
 // src/main.rs:4686-4698), fused with step 0's RMSNorm + gates.  Tile aux = band.
 struct EpiBand : TableTiles {
+  Row256Maps maps;  // 3-D maps over [T][nb][256]
   const float* bias;  // [nb][256]
-  float* x;           // [T*nb][256]
   int nb;
   RowNormParams np;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int band = t.aux;
-    row256_epilogue(t, x, bias + band * 256, nullptr, this->x, np, [&](int r) { return (t.row0 + r) * nb + band; });
+    row256_epilogue<true>(t, x, bias + band * 256, nullptr, maps, np, band,
+                          [&](int r) { return (t.row0 + r) * nb + band; });
   }
 };
 
 // Mask estimator layer 1: hidden = f16(tanh(acc + b1)) (mask_gemm1_f16,
 // src/main.rs:4816-4842).  Tile aux = group*4 + n-tile, group = stem*nb + band.
 struct EpiTanh : TableTiles {
-  const float* bias;  // [groups][1024]
-  __half* hidden;     // [groups*T][1024]
-  int T;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+  CUtensorMap out_map;  // hidden [groups][T][1024] fp16, box 32 x 32 x 1, 64-byte swizzle
+  const float* bias;    // [groups][1024]
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int group = t.aux >> 2, n0 = (t.aux & 3) * kBN;
-    const int rb = x.q * 32;
 #pragma unroll 1
-    for (int c = x.hsel * 128; c < x.hsel * 128 + 128; c += 32) {
+    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
       uint32_t v[32];
       tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
@@ -378,15 +514,14 @@ struct EpiTanh : TableTiles {
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
         const float4 b = ldg4(bb + 4 * j4);
-        w[2 * j4] = pack_f16x2(tanhf(__uint_as_float(v[4 * j4]) + b.x), tanhf(__uint_as_float(v[4 * j4 + 1]) + b.y));
+        w[2 * j4] =
+            pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4]) + b.x), tanh_fast(__uint_as_float(v[4 * j4 + 1]) + b.y));
         w[2 * j4 + 1] =
-            pack_f16x2(tanhf(__uint_as_float(v[4 * j4 + 2]) + b.z), tanhf(__uint_as_float(v[4 * j4 + 3]) + b.w));
+            pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4 + 2]) + b.z), tanh_fast(__uint_as_float(v[4 * j4 + 3]) + b.w));
       }
-      warp_store_rows<16>(x.stage, w, x.lane, [&](int rr) -> char* {
-        return rb + rr < t.rows
-                   ? reinterpret_cast<char*>(hidden + (static_cast<size_t>(group) * T + t.row0 + rb + rr) * 1024 + n0 + c)
-                   : nullptr;
-      });
+      uint32_t* buf = x.st.f16_buf();
+      stage_row<16>(buf, w, x.lane);
+      store_3d(&out_map, buf, n0 + c, t.row0 + x.q * 32, group, x.lane);
     }
   }
 };
@@ -405,15 +540,15 @@ struct EpiMask : TableTiles {
   const float2* spec;   // [2][T][1025]
   float2* out;          // [stems*2][T][1025]
   int T, n2tot;
-  __device__ void run(const TileDesc& t, const EpiCtx& x) const {
+  __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int r = t.row0 + x.row;
     const bool valid = x.row < t.rows;
     const int stem = t.aux >> 16, band = (t.aux >> 8) & 255, n0 = (t.aux & 255) * kBN;
     const int d_b = band_d[band], f0 = band_f0[band];
     const float* bb = bias2 + static_cast<size_t>(stem) * n2tot + band_o2[band] + n0;
-    const int c_end = min(x.hsel * 128 + 128, t.n);
+    const int c_end = min(x.c0 + kPartCols, t.n);
 #pragma unroll 1
-    for (int c = x.hsel * 128; c < c_end; c += 32) {
+    for (int c = x.c0; c < c_end; c += 32) {
       uint32_t v[32];
       tmem_ld32(x.tm + c, v);
       tmem_ld_wait(v);
@@ -454,8 +589,8 @@ struct EpiMask : TableTiles {
 // ---------------------------------------------------------------------------
 template <class Epi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Epi epi,
-                   int n_tiles, int* status) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ Epi epi, int n_tiles, int* status) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kBarOff);
@@ -543,15 +678,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ---------------- epilogue warps ----------------
-    const int ew = warp - 2;  // 0..7
+    const int ew = warp - 2;  // 0..kEpiWarps-1
     EpiCtx x;
     x.lane = lane;
     x.q = warp & 3;  // TMEM lane quadrant this warp may access
-    x.hsel = ew >> 2;
+    x.part = ew >> 2;
+    x.c0 = x.part * kPartCols;
     x.row = x.q * 32 + lane;
     uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kStagingOff);
-    x.stage = staging + ew * kStageWords;
-    x.peer = staging + (ew ^ 4) * kStageWords;
+    // buffers are laid out quadrant-major so the kParts warps of a quadrant are contiguous
+    x.quad = staging + x.q * kParts * kStageWords;
+    x.st.base = x.quad + x.part * kStageWords;
+    x.st.lane = lane;
+    x.st.phase = 0;
+    x.st.last_f32 = false;
     x.bar_id = 1 + x.q;
     int i = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
@@ -565,6 +705,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[slot]);
     }
+    if (lane == 0) tma_store_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -605,10 +747,15 @@ static cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const
 
 static int dense_tiles(int M, int N) { return ((M + kBM - 1) / kBM) * (N / kBN); }
 
-static RowNormParams no_norm() {
-  RowNormParams p{};
-  p.norm = 0;
-  return p;
+// fp16 [rows][cols] output map for 32 x 32 blocks (64-byte rows, 64-byte swizzle)
+static cudaError_t out_map16(CUtensorMap* m, const void* base, int cols, uint64_t rows) {
+  return make_map_2d(m, base, cols, rows, static_cast<uint64_t>(cols) * 2, 32, 32, MapElem::F16,
+                     CU_TENSOR_MAP_SWIZZLE_64B);
+}
+// fp32 [rows][cols] output map for 32 x 32 blocks (128-byte rows, 128-byte swizzle)
+static cudaError_t out_map32(CUtensorMap* m, const void* base, int cols, uint64_t rows) {
+  return make_map_2d(m, base, cols, rows, static_cast<uint64_t>(cols) * 4, 32, 32, MapElem::F32,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 static RowNormParams to_params(const RowNorm& n) {
@@ -617,7 +764,6 @@ static RowNormParams to_params(const RowNorm& n) {
   p.gamma = n.gamma;
   p.gate_w = n.gate_w;
   p.gate_b = n.gate_b;
-  p.h16 = n.h16;
   p.gates = n.gates;
   p.xb16 = n.xb16;
   p.T = n.T;
@@ -628,17 +774,17 @@ static RowNormParams to_params(const RowNorm& n) {
 cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, const float* cos, const float* sin,
                      __half* qkv, int M, int nb, int axis, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiQKV ep;
   cudaError_t e = make_map_2d(&ta, h16, 256, M, 256 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w, 256, 1536, 256 * 2, kBK, kBN);
+  if (e == cudaSuccess) e = out_map16(&ep.out_map, qkv, 1536, M);
   if (e != cudaSuccess) return e;
-  EpiQKV ep;
   ep.M = M;
   ep.n_tiles = 1536 / kBN;
   ep.kblocks = 256 / kBK;
   ep.bias16 = bias16;
   ep.cos = cos;
   ep.sin = sin;
-  ep.qkv = qkv;
   ep.nb = nb;
   ep.axis = axis;
   return launch_gemm(ta, tb, ep, dense_tiles(M, 1536), status, st);
@@ -647,52 +793,52 @@ cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, co
 cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const float* bias, const float* resid,
                               const float* gamma, float* out, __half* h16, int M, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiRow256 ep;
   cudaError_t e = make_map_2d(&ta, scaled16, 512, M, 512 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w, 512, 256, 512 * 2, kBK, kBN);
+  if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, out, 256, M);
+  if (e == cudaSuccess) e = out_map16(&ep.maps.h16_map, h16, 256, M);
   if (e != cudaSuccess) return e;
-  EpiOutNorm ep;
   ep.M = M;
   ep.n_tiles = 1;
   ep.kblocks = 512 / kBK;
   ep.bias = bias;
   ep.resid = resid;
-  ep.out = out;
-  ep.np = no_norm();
+  ep.np = RowNormParams{};
   ep.np.norm = 1;
   ep.np.gamma = gamma;
-  ep.np.h16 = h16;
   return launch_gemm(ta, tb, ep, dense_tiles(M, 256), status, st);
 }
 
 cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, __half* ff1, int M, int* status,
                           cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiGelu ep;
   cudaError_t e = make_map_2d(&ta, h16, 256, M, 256 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w1, 256, 1024, 256 * 2, kBK, kBN);
+  if (e == cudaSuccess) e = out_map16(&ep.out_map, ff1, 1024, M);
   if (e != cudaSuccess) return e;
-  EpiGelu ep;
   ep.M = M;
   ep.n_tiles = 1024 / kBN;
   ep.kblocks = 256 / kBK;
   ep.bias = b1;
-  ep.out = ff1;
-  ep.ldo = 1024;
   return launch_gemm(ta, tb, ep, dense_tiles(M, 1024), status, st);
 }
 
 cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2, const float* resid, float* x, int M,
                            const RowNorm& next, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiRow256 ep;
   cudaError_t e = make_map_2d(&ta, ff1, 1024, M, 1024 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w2, 1024, 256, 1024 * 2, kBK, kBN);
+  if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, x, 256, M);
+  if (e == cudaSuccess && next.h16) e = out_map16(&ep.maps.h16_map, next.h16, 256, M);
   if (e != cudaSuccess) return e;
-  EpiResid ep;
   ep.M = M;
   ep.n_tiles = 1;
   ep.kblocks = 1024 / kBK;
   ep.bias = b2;
   ep.resid = resid;
-  ep.out = x;
   ep.np = to_params(next);
   return launch_gemm(ta, tb, ep, dense_tiles(M, 256), status, st);
 }
@@ -701,15 +847,21 @@ cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, i
                            float* x, int T, int nb, const TileDesc* tiles, int n_tiles, const RowNorm& first,
                            int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiBand ep;
   cudaError_t e = make_map_2d(&ta, xn, xn_cols, T, static_cast<uint64_t>(xn_cols) * 2, kBK, kBM);
   if (e == cudaSuccess)
     e = make_map_2d(&tb, wband, wband_cols, static_cast<uint64_t>(nb) * 256, static_cast<uint64_t>(wband_cols) * 2,
                     kBK, kBN);
+  // token rows t*nb + band viewed as [T][nb][256]
+  if (e == cudaSuccess)
+    e = make_map_3d(&ep.maps.out_map, x, 256, nb, T, 256 * 4, static_cast<uint64_t>(nb) * 256 * 4, 32, 1, 32,
+                    MapElem::F32, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (e == cudaSuccess && first.h16)
+    e = make_map_3d(&ep.maps.h16_map, first.h16, 256, nb, T, 256 * 2, static_cast<uint64_t>(nb) * 256 * 2, 32, 1,
+                    32, MapElem::F16, CU_TENSOR_MAP_SWIZZLE_64B);
   if (e != cudaSuccess) return e;
-  EpiBand ep;
   ep.table = tiles;
   ep.bias = bias;
-  ep.x = x;
   ep.nb = nb;
   ep.np = to_params(first);
   return launch_gemm(ta, tb, ep, n_tiles, status, st);
@@ -718,14 +870,16 @@ cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, i
 cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __half* hidden, int T, int groups,
                        const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
+  EpiTanh ep;
   cudaError_t e = make_map_2d(&ta, xb16, 256, static_cast<uint64_t>(T) * kNumBands, 256 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w1, 256, static_cast<uint64_t>(groups) * 1024, 256 * 2, kBK, kBN);
+  // hidden viewed as [groups][T][1024] so a tile's rows never spill into the next group
+  if (e == cudaSuccess)
+    e = make_map_3d(&ep.out_map, hidden, 1024, T, groups, 1024 * 2, static_cast<uint64_t>(T) * 1024 * 2, 32, 32, 1,
+                    MapElem::F16, CU_TENSOR_MAP_SWIZZLE_64B);
   if (e != cudaSuccess) return e;
-  EpiTanh ep;
   ep.table = tiles;
   ep.bias = b1;
-  ep.hidden = hidden;
-  ep.T = T;
   return launch_gemm(ta, tb, ep, n_tiles, status, st);
 }
 

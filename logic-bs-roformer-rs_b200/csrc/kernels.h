@@ -40,11 +40,14 @@ struct RowNorm {
   int T = 0, nb = 0;
 };
 
-// TMA tensor maps (fp16, 128-byte swizzle, zero OOB fill).
+// TMA tensor maps (zero OOB fill).  Defaults: fp16 elements, 128-byte swizzle.
+enum class MapElem { F16, F32 };
 cudaError_t make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-                        uint32_t box_inner, uint32_t box_outer);
+                        uint32_t box_inner, uint32_t box_outer, MapElem elem = MapElem::F16,
+                        CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 cudaError_t make_map_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
-                        uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2);
+                        uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2, MapElem elem = MapElem::F16,
+                        CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // ---- GEMMs (gemm.cu) -------------------------------------------------------
 cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, const float* cos, const float* sin,
