@@ -11,10 +11,11 @@
 //   freq axis  two sequences (frames 2p, 2p+1) of nb = 62 bands packed into
 //              one 128-row tile (block-diagonal mask), a single key tile.
 // Pipeline (192 threads): warp 0 TMA (Q once, K/V double-buffered), warp 1
-// issues S = Q K^T (TMEM cols 0..127) and O += P V (TMEM cols 128..191, V as an
-// MN-major operand), warps 2..5 run the softmax with one query row per thread,
-// write P (fp16, 128-byte swizzled K-major) to shared memory, rescale O in
-// TMEM, and finally write f16(f16(O/l) * sigmoid(gate)).
+// issues S = Q K^T (TMEM cols 0..127) and O += P V (TMEM cols 128..191; P read
+// from TMEM cols 192..255, V an MN-major shared-memory operand), warps 2..5 run
+// the softmax with one query row per thread, write P (fp16 pairs) to TMEM,
+// rescale O in TMEM, and finally write f16(f16(O/l) * sigmoid(gate)).  Keeping
+// P in TMEM halves the shared-memory traffic of a key tile.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -25,13 +26,13 @@ constexpr int kTile = 16384;  // one [128][64] fp16 tile
 constexpr int kOffQ = 0;
 constexpr int kOffK = kTile;
 constexpr int kOffV = 3 * kTile;
-constexpr int kOffP = 5 * kTile;
-constexpr int kOffBar = 7 * kTile;
+constexpr int kOffBar = 5 * kTile;
 constexpr int kAttnSmem = kOffBar + 128;
 constexpr int kAttnThreads = 192;
 constexpr uint32_t kAttnTmemCols = 256;
 constexpr uint32_t kColS = 0;
 constexpr uint32_t kColO = 128;
+constexpr uint32_t kColP = 192;  // 128 keys of fp16 = 64 columns
 
 struct AttnArgs {
   const float* gates;  // [M][8]
@@ -128,12 +129,12 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
                      k > 0 ? 1u : 0u);
       };
       auto issue_pv = [&](int s, bool acc) {
-        const uint32_t sp = smem_u32(smem + kOffP);
         const uint32_t sv = smem_u32(smem + kOffV + s * kTile);
+        // A = P from TMEM: 16 keys per MMA = 8 packed columns
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ss(tmem + kColO, sdesc_sw128(sp + (kk >> 2) * kTile + (kk & 3) * 32, 1024, 16),
-                     sdesc_sw128(sv + kk * 2048, 1024, 0), id_o, (acc || kk > 0) ? 1u : 0u);
+          mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
+                     (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
       if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag, a.status);
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     const uint32_t tO = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColO;
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
     const int rseq = r / nb;                        // freq axis: which packed sequence
-    uint8_t* sP = smem + kOffP;
+    const uint32_t tP = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColP;
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
@@ -179,20 +180,24 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       const int lo = time_axis ? 0 : rseq * nb;
       const int hi = time_axis ? min(128, T - key0) : lo + nb;
       const bool full = lo == 0 && hi >= 128;  // warp-uniform on the time axis
-      float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tS + c, v);
-        tmem_ld_wait(v);
-        if (full) {
+      // the whole S row (128 fp32) in registers: four loads, one wait
+      uint32_t s[4][32];
 #pragma unroll
-          for (int k = 0; k < 32; ++k) mx = fmaxf(mx, __uint_as_float(v[k]));
-        } else {
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(tS + q4 * 32, s[q4]);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld_wait(s[q4]);
+      float mx = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+          for (int k = 0; k < 32; ++k) mx = fmaxf(mx, __uint_as_float(s[q4][k]));
+      } else {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
 #pragma unroll
           for (int k = 0; k < 32; ++k)
-            if (c + k >= lo && c + k < hi) mx = fmaxf(mx, __uint_as_float(v[k]));
-        }
+            if (q4 * 32 + k >= lo && q4 * 32 + k < hi) mx = fmaxf(mx, __uint_as_float(s[q4][k]));
       }
       const float m_new = fmaxf(m_run, mx);
       // Keep the running reference max unless the row max grew by more than
@@ -209,6 +214,28 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
         m_next = m_run;
       }
       const float msc = m_use * sc;
+      // p = 2^(s*sc - m*sc) into fp16 pairs: packed fp32x2 FMA for the exponent
+      // argument and packed adds for the row sum, one MUFU ex2 per element.
+      // Computed before waiting for PV_{j-1}, so it overlaps that MMA.
+      uint32_t w[64];
+      float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const int c0 = q4 * 32 + 2 * k;
+          const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(s[q4][2 * k]), __uint_as_float(s[q4][2 * k + 1])),
+                                       make_float2(sc, sc), make_float2(-msc, -msc));
+          float2 p = make_float2(ex2(a2.x), ex2(a2.y));
+          if (!full) {
+            p.x = (c0 >= lo && c0 < hi) ? p.x : 0.f;
+            p.y = (c0 + 1 >= lo && c0 + 1 < hi) ? p.y : 0.f;
+          }
+          sum2 = __fadd2_rn(sum2, p);
+          w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
+        }
+      }
+      const float sum = sum2.x + sum2.y;
       if (j > 0) {
         // PV_{j-1} must be done before O is rescaled and P is overwritten
         ok = mbar_wait(pv_done, (j - 1) & 1, abort_flag, a.status);
@@ -221,50 +248,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
             tmem_ld32(tO + c, v);
             tmem_ld_wait(v);
 #pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] = __float_as_uint(__uint_as_float(v[k]) * corr);
+            for (int k = 0; k < 16; ++k) {
+              const float2 o = __fmul2_rn(make_float2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1])),
+                                          make_float2(corr, corr));
+              v[2 * k] = __float_as_uint(o.x);
+              v[2 * k + 1] = __float_as_uint(o.y);
+            }
             tmem_st32(tO + c, v);
           }
           tmem_st_wait();
         }
       }
-      float sum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 128; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tS + c, v);
-        tmem_ld_wait(v);
-        uint32_t w[16];
-        if (full) {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float p0 = ex2(__uint_as_float(v[2 * k]) * sc - msc);
-            const float p1 = ex2(__uint_as_float(v[2 * k + 1]) * sc - msc);
-            sum += p0 + p1;
-            w[k] = pack_f16x2(p0, p1);
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const int c0 = c + 2 * k;
-            const float p0 = (c0 >= lo && c0 < hi) ? ex2(__uint_as_float(v[2 * k]) * sc - msc) : 0.f;
-            const float p1 = (c0 + 1 >= lo && c0 + 1 < hi) ? ex2(__uint_as_float(v[2 * k + 1]) * sc - msc) : 0.f;
-            sum += p0 + p1;
-            w[k] = pack_f16x2(p0, p1);
-          }
-        }
-        // row r of the K-major [128 rows][128 keys] P operand: key block c/64,
-        // 16-byte chunk ((c%64)/8 + i) swizzled with (r & 7)
-        uint8_t* base = sP + (c >> 6) * kTile + r * 128;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int chunk = ((c & 63) >> 3) + i;
-          *reinterpret_cast<uint4*>(base + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
+      // P row r into TMEM lane r: column c holds keys (2c, 2c+1)
+      {
+        uint32_t* w0 = w;
+        uint32_t* w1 = w + 32;
+        tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(w0));
+        tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(w1));
+        tmem_st_wait();
       }
       l_run = l_run * corr + sum;
       m_run = m_next;
-      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(p_full);
     }

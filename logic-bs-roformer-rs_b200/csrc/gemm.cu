@@ -270,17 +270,18 @@ struct EpiQKV : DenseTiles {
         for (int j = 0; j < 4; ++j) {
           const int k = 8 * j4 + 2 * j;
           const float2 eo = __fadd2_rn(f2(__uint_as_float(v[k]), __uint_as_float(v[k + 1])), f2(bb[2 * j], bb[2 * j + 1]));
-          const uint32_t q16 = pack_f16x2(eo.x, eo.y);
           if (rot) {
-            // (e c - o s, o c + e s) from the fp16-rounded pair, products rounded
-            // separately like the reference's rope kernels
-            const float2 r = unpack_f16x2(q16);
-            const float2 p1 = __fmul2_rn(r, f2(cc[j], cc[j]));
-            const float2 p2 = __fmul2_rn(f2(r.y, r.x), f2(-ss[j], ss[j]));
+            // (e c - o s, o c + e s), products rounded separately like the
+            // reference's rope kernels, applied to the fp32 pair and rounded to
+            // fp16 once (the reference rounds before and after the rotation;
+            // one fp16 conversion per pair instead of two keeps the XU pipe,
+            // which executes the conversions, off the critical path)
+            const float2 p1 = __fmul2_rn(eo, f2(cc[j], cc[j]));
+            const float2 p2 = __fmul2_rn(f2(eo.y, eo.x), f2(-ss[j], ss[j]));
             const float2 o2 = __fadd2_rn(p1, p2);
             w[4 * j4 + j] = pack_f16x2(o2.x, o2.y);
           } else {
-            w[4 * j4 + j] = q16;
+            w[4 * j4 + j] = pack_f16x2(eo.x, eo.y);
           }
         }
       }
