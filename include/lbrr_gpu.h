@@ -180,6 +180,22 @@ int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const float* b2,
 
 int lbrr_op_sync(void* stream);
 
+/* Feed-forward half of a RoFormer step (FF1 + GELU, then FF2 + bias +
+ * residual into x) that allocates no device memory; it has no counterpart in
+ * the reference.  For callers that cannot call cudaMalloc: a real-time audio
+ * host calling from its render thread, or an application that gives the
+ * library a fixed device-memory budget.  The fp16 hidden activations use a
+ * file-scope static device array of 8192 x 1024 halves (16 MiB, held by every
+ * GPU that loads the library until exit); rows > 8192 are rejected with
+ * LBRR_ERR_INVALID.  The first call on a device resolves the array's address
+ * (with that device current) and should come before any stream capture.
+ * Calls share the array: work of calls that overlaps on the GPU races.  The
+ * call returns after its work on `stream` has finished and reports a kernel
+ * status as LBRR_ERR_DEVICE.  Shapes: h16 [rows][256], w1 [1024][256],
+ * b1 [1024], w2 [256][1024], b2 [256], resid and x [rows][256] fp32. */
+int lbrr_op_feed_forward_noalloc(const uint16_t* h16, const uint16_t* w1_16, const float* b1, const uint16_t* w2_16,
+                                 const float* b2, const float* resid, float* x, int64_t rows, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

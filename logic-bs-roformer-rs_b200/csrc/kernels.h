@@ -5,6 +5,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+// Sets the thread-local message returned by lbrr_last_error and returns code
+// (defined in engine.cu; used by the other translation units).
+extern "C" int lbrr_set_error_for_host(int code, const char* msg);
+
 namespace lbrr {
 
 constexpr int kNumBands = 62;
