@@ -97,6 +97,15 @@ int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size
 /* Same, reading a .safetensors file (F32 tensors; src/weights.rs:25-55). */
 int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path);
 
+/* Host-only checkpoint validation with exactly the checks of
+ * lbrr_engine_load_weights (no device needed); replaces `lbrr --check-weights`
+ * (src/main.rs:97, ModelWeights::load src/weights.rs:307-447). */
+int lbrr_check_weights(const lbrr_weight_view* views, size_t n);
+
+/* Host-only validation of a .safetensors file: header parse, F32 dtypes, byte
+ * lengths, then lbrr_check_weights on its tensors. */
+int lbrr_check_safetensors(const char* path);
+
 /* One chunk, device buffers on the engine's device, stream-ordered on `stream`
  * (NULL = the engine's stream).  x_dev: [len][2] fp32, stems_dev: [6][2][len]
  * fp32.  len must satisfy n_fft/2 < len <= max_chunk_samples (src/main.rs:7263).

@@ -249,6 +249,43 @@ static int check_desc(const lbrr_model_desc* d) {
 
 static int T_of(int64_t len) { return static_cast<int>(len / kHop + 1); }
 
+// Placeholder base for laying out the weight arena before (or without) a device
+// allocation; only differences from it are ever used.
+static char* const kLayoutBase = reinterpret_cast<char*>(static_cast<uintptr_t>(1) << 30);
+
+// Lay out the weight arena at base W (1024-aligned blocks) and point the
+// engine's weight pointers into it; returns the arena size in bytes.
+static size_t carve_weights(lbrr_engine* e, char* W) {
+  const BandGeom& G = geom();
+  Carver w;
+  auto h16 = [&](size_t n) { return reinterpret_cast<__half*>(W + w.take<__half>(n)); };
+  auto f32 = [&](size_t n) { return reinterpret_cast<float*>(W + w.take<float>(n)); };
+  for (int k = 0; k < 2 * kDepth; ++k) {
+    StepWeights& sw = e->steps[k];
+    sw.wqkv = h16(1536 * 256);
+    sw.wo = h16(256 * 512);
+    sw.w1 = h16(1024 * 256);
+    sw.w2 = h16(256 * 1024);
+    sw.norm_g = f32(256);
+    sw.gate_w = f32(8 * 256);
+    sw.gate_b = f32(8);
+    sw.ff_g = f32(256);
+    sw.b1 = f32(1024);
+    sw.b2 = f32(256);
+  }
+  e->qkv_bias16 = f32(1536);
+  e->out_bias = f32(256);
+  e->final_g = f32(256);
+  e->band_w = h16(static_cast<size_t>(kNumBands) * 256 * G.kpad_max);
+  e->band_b = f32(kNumBands * 256);
+  e->band_g = f32(G.offs[kNumBands]);
+  e->mask_w1 = h16(static_cast<size_t>(kStems) * kNumBands * 1024 * 256);
+  e->mask_b1 = f32(static_cast<size_t>(kStems) * kNumBands * 1024);
+  e->mask_w2 = h16(static_cast<size_t>(kStems) * G.n2tot * 1024);
+  e->mask_b2 = f32(static_cast<size_t>(kStems) * G.n2tot);
+  return align_up(w.off, 1024);
+}
+
 extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64_t max_len, lbrr_engine** out) {
   if (!out) return fail(LBRR_ERR_INVALID, "out is NULL");
   *out = nullptr;
@@ -269,29 +306,8 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   e->max_T = T_of(max_len);
   const BandGeom& G = geom();
   const size_t T = e->max_T, M = T * kNumBands;
-  // ---- weights arena ----
-  Carver w;
-  size_t o_steps[2 * kDepth][10];
-  for (int s = 0; s < 2 * kDepth; ++s) {
-    o_steps[s][0] = w.take<__half>(1536 * 256);
-    o_steps[s][1] = w.take<__half>(256 * 512);
-    o_steps[s][2] = w.take<__half>(1024 * 256);
-    o_steps[s][3] = w.take<__half>(256 * 1024);
-    o_steps[s][4] = w.take<float>(256);
-    o_steps[s][5] = w.take<float>(8 * 256);
-    o_steps[s][6] = w.take<float>(8);
-    o_steps[s][7] = w.take<float>(256);
-    o_steps[s][8] = w.take<float>(1024);
-    o_steps[s][9] = w.take<float>(256);
-  }
-  const size_t o_qb = w.take<float>(1536), o_ob = w.take<float>(256), o_fg = w.take<float>(256);
-  const size_t o_bw = w.take<__half>(static_cast<size_t>(kNumBands) * 256 * G.kpad_max);
-  const size_t o_bb = w.take<float>(kNumBands * 256), o_bg = w.take<float>(G.offs[kNumBands]);
-  const size_t o_m1 = w.take<__half>(static_cast<size_t>(kStems) * kNumBands * 1024 * 256);
-  const size_t o_mb1 = w.take<float>(static_cast<size_t>(kStems) * kNumBands * 1024);
-  const size_t o_m2 = w.take<__half>(static_cast<size_t>(kStems) * G.n2tot * 1024);
-  const size_t o_mb2 = w.take<float>(static_cast<size_t>(kStems) * G.n2tot);
-  e->warena_bytes = align_up(w.off, 1024);
+  // ---- weights arena (sized first, pointers assigned after the allocation) ----
+  e->warena_bytes = carve_weights(e, kLayoutBase);
   // ---- scratch arena ----
   Carver s;
   const size_t o_win = s.take<float>(kNfft), o_fr = s.take<float>(2 * T * kNfft), o_sp = s.take<float2>(2 * T * kBins);
@@ -319,31 +335,8 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   if (ce == cudaSuccess) ce = cudaMallocHost(&e->pin_in, 2 * max_len * sizeof(float));
   if (ce == cudaSuccess) ce = cudaMallocHost(&e->pin_out, 2 * kStems * max_len * sizeof(float));
   if (ce != cudaSuccess) return cleanup(fail(LBRR_ERR_CUDA, std::string("engine allocation: ") + cudaGetErrorString(ce)));
-  char* W = static_cast<char*>(e->warena);
+  carve_weights(e, static_cast<char*>(e->warena));
   char* S = static_cast<char*>(e->sarena);
-  for (int k = 0; k < 2 * kDepth; ++k) {
-    StepWeights& sw = e->steps[k];
-    sw.wqkv = reinterpret_cast<__half*>(W + o_steps[k][0]);
-    sw.wo = reinterpret_cast<__half*>(W + o_steps[k][1]);
-    sw.w1 = reinterpret_cast<__half*>(W + o_steps[k][2]);
-    sw.w2 = reinterpret_cast<__half*>(W + o_steps[k][3]);
-    sw.norm_g = reinterpret_cast<float*>(W + o_steps[k][4]);
-    sw.gate_w = reinterpret_cast<float*>(W + o_steps[k][5]);
-    sw.gate_b = reinterpret_cast<float*>(W + o_steps[k][6]);
-    sw.ff_g = reinterpret_cast<float*>(W + o_steps[k][7]);
-    sw.b1 = reinterpret_cast<float*>(W + o_steps[k][8]);
-    sw.b2 = reinterpret_cast<float*>(W + o_steps[k][9]);
-  }
-  e->qkv_bias16 = reinterpret_cast<float*>(W + o_qb);
-  e->out_bias = reinterpret_cast<float*>(W + o_ob);
-  e->final_g = reinterpret_cast<float*>(W + o_fg);
-  e->band_w = reinterpret_cast<__half*>(W + o_bw);
-  e->band_b = reinterpret_cast<float*>(W + o_bb);
-  e->band_g = reinterpret_cast<float*>(W + o_bg);
-  e->mask_w1 = reinterpret_cast<__half*>(W + o_m1);
-  e->mask_b1 = reinterpret_cast<float*>(W + o_mb1);
-  e->mask_w2 = reinterpret_cast<__half*>(W + o_m2);
-  e->mask_b2 = reinterpret_cast<float*>(W + o_mb2);
   e->band_tab = reinterpret_cast<int*>(S + o_tab);
   e->band_f0 = reinterpret_cast<int*>(S + o_f0);
   e->band_d = reinterpret_cast<int*>(S + o_d);
@@ -455,9 +448,13 @@ void pack16(uint16_t* dst, const float* src, size_t n) {
 }
 }  // namespace
 
-extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size_t n) {
-  if (!e || (!views && n)) return fail(LBRR_ERR_INVALID, "NULL engine or views");
-  DeviceGuard g(e->device);
+// Validate a checkpoint (every one of the 1989 keys exactly once with its exact
+// size, shared biases bit-equal, analytic rotary freqs, no extra key;
+// src/weights.rs:307-432) and build the packed host image of the weight arena
+// whose pointers e holds relative to `base`.
+static int build_weight_image(const lbrr_engine* e, const char* base, const lbrr_weight_view* views, size_t n,
+                              std::vector<uint8_t>& host) {
+  if (!views && n) return fail(LBRR_ERR_INVALID, "NULL views");
   const BandGeom& G = geom();
   ViewMap vm;
   for (size_t i = 0; i < n; ++i) {
@@ -465,9 +462,8 @@ extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* 
     if (!vm.m.emplace(views[i].name, &views[i]).second)
       return fail(LBRR_ERR_WEIGHTS, std::string("duplicate tensor ") + views[i].name);
   }
-  // host image of the weight arena
-  std::vector<uint8_t> host(e->warena_bytes, 0);
-  auto hp = [&](const void* dev_ptr) { return host.data() + (static_cast<const char*>(dev_ptr) - static_cast<const char*>(e->warena)); };
+  host.assign(e->warena_bytes, 0);
+  auto hp = [&](const void* p) { return host.data() + (static_cast<const char*>(p) - base); };
   const float* sq = vm.take("linear_62_bias_0", 1536);
   const float* so = vm.take("linear_64_bias_0", 256);
   if (!vm.err.empty()) return fail(LBRR_ERR_WEIGHTS, vm.err);
@@ -561,9 +557,24 @@ extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* 
   for (auto& kv : vm.m)
     if (!vm.used.count(kv.first))
       return fail(LBRR_ERR_WEIGHTS, "unconsumed key " + kv.first);
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size_t n) {
+  if (!e) return fail(LBRR_ERR_INVALID, "NULL engine");
+  std::vector<uint8_t> host;
+  if (int rc = build_weight_image(e, static_cast<const char*>(e->warena), views, n, host)) return rc;
+  DeviceGuard g(e->device);
   CK(cudaMemcpy(e->warena, host.data(), host.size(), cudaMemcpyHostToDevice));
   e->weights_loaded = true;
   return LBRR_OK;
+}
+
+extern "C" int lbrr_check_weights(const lbrr_weight_view* views, size_t n) {
+  lbrr_engine layout;  // host-only: pointers laid out at a placeholder base, nothing allocated on a device
+  layout.warena_bytes = carve_weights(&layout, kLayoutBase);
+  std::vector<uint8_t> host;
+  return build_weight_image(&layout, kLayoutBase, views, n, host);
 }
 
 // ---------------------------------------------------------------------------

@@ -191,8 +191,11 @@ struct Parser {
 extern "C" const char* lbrr_last_error(void);
 extern "C" int lbrr_set_error_for_host(int code, const char* msg);
 
-extern "C" int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path) {
-  if (!e || !path) return lbrr_set_error_for_host(LBRR_ERR_INVALID, "NULL engine or path");
+namespace {
+// Parse the file into fp32 buffers and name-keyed views (views point into bufs
+// and metas, which the caller keeps alive).
+int read_views(const char* path, std::vector<Meta>& metas, std::vector<std::vector<float>>& bufs,
+               std::vector<lbrr_weight_view>& views) {
   FILE* f = std::fopen(path, "rb");
   if (!f) return lbrr_set_error_for_host(LBRR_ERR_WEIGHTS, (std::string("open ") + path).c_str());
   uint8_t lb[8];
@@ -229,11 +232,11 @@ extern "C" int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path) {
   }
   std::fclose(f);
   Parser p{header.data(), header.size()};
-  std::vector<Meta> metas;
+  metas.clear();
   if (!p.header(metas)) return lbrr_set_error_for_host(LBRR_ERR_WEIGHTS, ("safetensors header: " + p.err).c_str());
   // copy each tensor into an aligned fp32 buffer (offsets are only byte-aligned)
-  std::vector<std::vector<float>> bufs(metas.size());
-  std::vector<lbrr_weight_view> views(metas.size());
+  bufs.assign(metas.size(), std::vector<float>());
+  views.assign(metas.size(), lbrr_weight_view{});
   for (size_t k = 0; k < metas.size(); ++k) {
     const Meta& m = metas[k];
     if (m.dtype != "F32")
@@ -248,5 +251,24 @@ extern "C" int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path) {
     views[k].data = bufs[k].data();
     views[k].numel = static_cast<int64_t>(numel);
   }
+  return LBRR_OK;
+}
+}  // namespace
+
+extern "C" int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path) {
+  if (!e || !path) return lbrr_set_error_for_host(LBRR_ERR_INVALID, "NULL engine or path");
+  std::vector<Meta> metas;
+  std::vector<std::vector<float>> bufs;
+  std::vector<lbrr_weight_view> views;
+  if (int rc = read_views(path, metas, bufs, views)) return rc;
   return lbrr_engine_load_weights(e, views.data(), views.size());
+}
+
+extern "C" int lbrr_check_safetensors(const char* path) {
+  if (!path) return lbrr_set_error_for_host(LBRR_ERR_INVALID, "NULL path");
+  std::vector<Meta> metas;
+  std::vector<std::vector<float>> bufs;
+  std::vector<lbrr_weight_view> views;
+  if (int rc = read_views(path, metas, bufs, views)) return rc;
+  return lbrr_check_weights(views.data(), views.size());
 }

@@ -70,6 +70,8 @@ def lib() -> C.CDLL:
         "lbrr_engine_create": ([C.c_int, C.POINTER(ModelDesc), i64, C.POINTER(vp)], C.c_int),
         "lbrr_engine_load_weights": ([vp, C.POINTER(WeightView), C.c_size_t], C.c_int),
         "lbrr_engine_load_safetensors": ([vp, C.c_char_p], C.c_int),
+        "lbrr_check_weights": ([C.POINTER(WeightView), C.c_size_t], C.c_int),
+        "lbrr_check_safetensors": ([C.c_char_p], C.c_int),
         "lbrr_forward_chunk": ([vp, vp, i64, vp, vp], C.c_int),
         "lbrr_forward_chunk_host": ([vp, vp, i64, vp], C.c_int),
         "lbrr_forward_trunk": ([vp, vp, i64, C.c_int, vp, vp], C.c_int),
@@ -99,7 +101,7 @@ def lib() -> C.CDLL:
 # Every symbol include/lbrr_gpu.h declares (checked by the CPU test suite).
 HEADER_SYMBOLS = [
     "lbrr_last_error", "lbrr_abi_version", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
-    "lbrr_engine_load_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
+    "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
     "lbrr_engine_sync", "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
     "lbrr_op_qkv_rope", "lbrr_op_attention", "lbrr_op_outproj_norm", "lbrr_op_ff1_gelu", "lbrr_op_ff2_resid",
     "lbrr_op_sync", "lbrr_op_feed_forward_noalloc",
@@ -134,6 +136,33 @@ def default_model():
     return d
 
 
+def _weight_views(weights: dict):
+    """fp32 copies of {name: array} and the lbrr_weight_view array pointing at them."""
+    keep, views = [], (WeightView * len(weights))()
+    for i, (name, t) in enumerate(weights.items()):
+        a = np.ascontiguousarray(np.asarray(t.detach().cpu() if hasattr(t, "detach") else t, dtype=np.float32))
+        keep.append(a)
+        views[i].name = name.encode()
+        views[i].data = a.ctypes.data_as(C.POINTER(C.c_float))
+        views[i].numel = a.size
+    return keep, views
+
+
+def check_weights(weights: dict):
+    """Validate a checkpoint on the host only (no GPU needed): the reference's
+    `--check-weights` mode (src/main.rs:332-365, ModelWeights::load in
+    src/weights.rs:307-447).  Raises LbrrError(ERR_WEIGHTS) naming the first
+    bad tensor."""
+    keep, views = _weight_views(weights)
+    check(lib().lbrr_check_weights(views, len(weights)))
+    del keep
+
+
+def check_safetensors(path):
+    """Parse and validate a .safetensors checkpoint on the host only."""
+    check(lib().lbrr_check_safetensors(str(path).encode()))
+
+
 class Engine:
     """One GPU's engine: weights, scratch, cuFFT plans and a stream."""
 
@@ -149,13 +178,7 @@ class Engine:
     def upload_weights(self, weights: dict):
         """Validate and upload a checkpoint given as {name: fp32 array/tensor}
         (ModelWeights::load + upload_weights, src/weights.rs:307-447, src/main.rs:6045-6077)."""
-        keep, views = [], (WeightView * len(weights))()
-        for i, (name, t) in enumerate(weights.items()):
-            a = np.ascontiguousarray(np.asarray(t.detach().cpu() if hasattr(t, "detach") else t, dtype=np.float32))
-            keep.append(a)
-            views[i].name = name.encode()
-            views[i].data = a.ctypes.data_as(C.POINTER(C.c_float))
-            views[i].numel = a.size
+        keep, views = _weight_views(weights)
         check(lib().lbrr_engine_load_weights(self.handle, views, len(weights)))
 
     def load_safetensors(self, path):
