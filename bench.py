@@ -43,6 +43,10 @@ CHUNK = 588800
 SONG_LEN = 7959168  # 180.48 s at 44.1 kHz
 SR = 44100
 METRIC = "ms/588800-sample chunk"
+# this repository's kernels per chunk forward: frames, band_norm, band-split GEMM,
+# 24 x (QKV, attention, out-proj, FF1, FF2), mask GEMM1, mask GEMM2, ISTFT
+# (the two cuFFT executions are library kernels and not counted)
+LAUNCHES_PER_CHUNK = 3 + 24 * 5 + 3
 UNIT = "ms/chunk"
 
 
@@ -118,8 +122,8 @@ class ClockSampler:
 # our arm
 # ---------------------------------------------------------------------------
 def make_inputs(seed=0):
-    from oracle import bsroformer_ref as R
-    return R.make_weights(seed=0), R.synth_audio(CHUNK, seed=seed)
+    from lbrr import synthetic
+    return synthetic.checkpoint(seed=0), synthetic.audio(CHUNK, seed=seed)
 
 
 def time_dominant_kernel(torch, lbrr, T=1151, iters=10):
@@ -286,7 +290,7 @@ def run_ours(args, rank, world, local_rank):
                        "l2": "flushed between steps (256 MiB write outside the timed events)"},
             "e2e": {"value": round(e2e_ms / world, 4), "unit": UNIT, "h2d_bytes_per_step": CHUNK * 2 * 4 * world,
                     "d2h_bytes_per_step": 6 * 2 * CHUNK * 4 * world},
-            "gpu_launches": 151 * args.steps * world,
+            "gpu_launches": LAUNCHES_PER_CHUNK * args.steps * world,
             "roofline": {"kernel": "attention time axis (attn_kernel, T=1151, 496 sequences)", "bound": "tensor",
                          "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["tflops"], 4), "traffic": traffic,
@@ -307,61 +311,35 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_song(torch, lbrr, eng, rank, world, dist):
-    """180.48 s song, reference chunk plan (15 chunks).  1 GPU: lbrr_separate_song.
-    N GPUs: chunk i on rank i % N, waveforms gathered to rank 0 (NCCL), accumulated
-    there in chunk order with the same fade/normalisation as the single-GPU path."""
-    from oracle import bsroformer_ref as R
-    audio = R.synth_audio(SONG_LEN, seed=42)
-    starts = R.chunk_starts(SONG_LEN)
+    """180.48 s song, reference chunk plan (15 chunks), from host audio to host
+    stems.  1 GPU: lbrr_separate_song.  N GPUs: lbrr.song.separate_ranks (chunk
+    i on rank i % N, waveforms sent to rank 0 over NCCL, overlap-added there in
+    chunk order).  Wall time around the whole call, max over ranks."""
+    from lbrr import song, synthetic
+    audio = synthetic.audio(SONG_LEN, seed=42)
+    starts = song.chunk_starts(SONG_LEN)
+    info = {"audio_seconds": SONG_LEN / SR, "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440"}
     if world == 1:
         lbrr.separate([eng], audio)  # warm
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         lbrr.separate([eng], audio)
         dt = time.perf_counter() - t0
-        return {"seconds": round(dt, 4), "audio_seconds": SONG_LEN / SR, "rtf": round(dt / (SONG_LEN / SR), 6),
-                "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440"}
-    # multi-rank: each rank forwards its chunks; rank 0 receives and stitches
-    needed = R.BORDER + SONG_LEN
-    xp = R.reflect_pad(audio, R.BORDER, starts[-1] + R.CHUNK - needed)
-    buf = torch.empty(6, 2, R.CHUNK, device="cuda")
-    recv = torch.empty(6, 2, R.CHUNK, device="cuda")
-    fade = torch.from_numpy(R.fade_window()).cuda()
+        return {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info}
+
+    def forward(x, y):
+        eng.bench_forward(x, y, stream=torch.cuda.current_stream())
+
     dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    result = torch.zeros(12, needed, device="cuda") if rank == 0 else None
-    counter = torch.zeros(needed, device="cuda") if rank == 0 else None
-    for i, s in enumerate(starts):
-        owner = i % world
-        if owner == rank:
-            xin = torch.from_numpy(np.ascontiguousarray(xp[:, s:s + R.CHUNK].T)).cuda()
-            eng.bench_forward(xin, buf)
-            eng.sync()
-            if rank != 0:
-                dist.send(buf, dst=0)
-        if rank == 0:
-            y = buf if owner == 0 else recv
-            if owner != 0:
-                dist.recv(recv, src=owner)
-            w = fade.clone()
-            if i == 0:
-                w[:R.BORDER] = 1
-            if i == len(starts) - 1:
-                w[-R.BORDER:] = 1
-            take = min(R.CHUNK, needed - s)
-            result[:, s:s + take] += y.reshape(12, -1)[:, :take] * w[:take]
-            counter[s:s + take] += w[:take] * w[:take]
-    if rank == 0:
-        out = (result / counter.clamp_min(1e-8))[:, R.BORDER:needed]
-        out.cpu()
+    song.separate_ranks(forward, audio, rank, world, dist, "cuda")
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
     t = torch.tensor([dt], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     dt = float(t.item())
-    return {"seconds": round(dt, 4), "audio_seconds": SONG_LEN / SR, "rtf": round(dt / (SONG_LEN / SR), 6),
-            "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440",
+    return {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info,
             "exchange": "per-chunk waveform [6][2][588800] fp32 sent to rank 0 over NCCL"}
 
 
