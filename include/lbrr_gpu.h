@@ -107,7 +107,8 @@ int lbrr_check_weights(const lbrr_weight_view* views, size_t n);
 int lbrr_check_safetensors(const char* path);
 
 /* One chunk, device buffers on the engine's device, stream-ordered on `stream`
- * (NULL = the engine's stream).  x_dev: [len][2] fp32, stems_dev: [6][2][len]
+ * (NULL = the engine's own stream; to order after work on the legacy default
+ * stream pass cudaStreamLegacy).  x_dev: [len][2] fp32, stems_dev: [6][2][len]
  * fp32.  len must satisfy n_fft/2 < len <= max_chunk_samples (src/main.rs:7263).
  * Replaces bench_forward + istft_ola (src/main.rs:7014-7162, :7303-7306). */
 int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);

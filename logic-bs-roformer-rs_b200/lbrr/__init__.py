@@ -122,10 +122,18 @@ def _ptr(t):
     return t.data_ptr()
 
 
+CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream named explicitly
+
+
 def _stream(stream):
+    """None -> NULL (the engine's own stream for engine calls).  A torch stream
+    whose handle is 0 is the legacy default stream: it is passed as
+    cudaStreamLegacy, because a NULL handle would put engine work on the
+    engine's stream, unordered with the caller's default-stream work."""
     if stream is None:
         return None
-    return stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    h = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream)
+    return h if h else CUDA_STREAM_LEGACY
 
 
 def default_model():
