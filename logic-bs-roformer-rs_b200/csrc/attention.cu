@@ -317,6 +317,302 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     tmem_dealloc(tmem, kAttnTmemCols);
   }
 }
+// ---------------------------------------------------------------------------
+// Time axis: two query tiles per CTA, ping-pong between tensor core and softmax
+// ---------------------------------------------------------------------------
+// One CTA (1 per SM, 384 threads) owns query tiles 2x and 2x+1 of one
+// (band, head) sequence; they share every K/V tile (3-stage TMA ring).  TMEM
+// (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383, P0
+// 384..447, P1 448..511.  Warpgroup 0 (warps 0..3) runs the softmax of slot
+// 0, warpgroup 1 (warps 4..7) that of slot 1, one query row per thread (warp
+// w reads TMEM lanes 32*(w%4)..); in warpgroup 2 warp 8 loads and warp 9
+// issues the MMAs.  As soon as slot s holds S_s(j) in registers the MMA warp
+// computes S_s(j+1) into the same columns, and once P_s(j) is written,
+// O_s += P_s V_j, so the tensor core works while both softmaxes run.  The
+// softmax warpgroups take 224 registers per thread from warpgroup 2
+// (setmaxnreg), enough for a whole S row and its fp16 P without spilling.
+constexpr int kT2Threads = 384;
+constexpr int kT2WarpTma = 8, kT2WarpMma = 9;
+constexpr int kT2RegsSoftmax = 224, kT2RegsOther = 48;
+constexpr int kT2Stages = 3;
+constexpr int kT2OffQ = 0;
+constexpr int kT2OffKV = 2 * kTile;  // stage st: K at +2*st*kTile, V at +(2*st+1)*kTile
+constexpr int kT2OffBar = kT2OffKV + kT2Stages * 2 * kTile;
+constexpr int kT2Smem = kT2OffBar + 256;
+constexpr uint32_t kT2TmemCols = 512;
+__device__ __forceinline__ uint32_t t2_col_s(int slot) { return slot * 128u; }
+__device__ __forceinline__ uint32_t t2_col_o(int slot) { return 256u + slot * 64u; }
+__device__ __forceinline__ uint32_t t2_col_p(int slot) { return 384u + slot * 64u; }
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__global__ void __launch_bounds__(kT2Threads, 1)
+    attn_time_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2OffBar);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;    // [kT2Stages]
+  uint64_t* kv_empty = bars + 4;   // [kT2Stages]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* p_full = bars + 9;     // [2]
+  uint64_t* o_done = bars + 11;    // [2]
+  uint64_t* s_free = bars + 13;    // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) report_status(a.status, kDevSmemMisaligned);
+    return;
+  }
+  const int nb = a.nb, T = a.T, nk = a.nk;
+  const int head = blockIdx.y & 7, band = blockIdx.y >> 3;
+  const int qt0 = blockIdx.x * 2;
+  const int nslots = (qt0 + 1) * 128 < T ? 2 : 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kT2Stages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
+      mbar_init(&s_free[i], 128);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kT2WarpTma && lane == 0) tma_prefetch(&tm);
+  if (warp == kT2WarpMma) {
+    tmem_alloc(tmem_slot, kT2TmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Register split, 2 x 128 x 224 + 128 x 48 <= 384 x 168 launch registers
+  // (the launcher checks the compiled count before the first launch); each
+  // role changes its own warpgroup's count at the top of its branch.
+  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kT2RegsOther));
+  if (warp == kT2WarpTma) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, nslots * kTile);
+      for (int s = 0; s < nslots; ++s)
+        tma_load_3d(smem + kT2OffQ + s * kTile, &tm, q_full, head * 64, band, (qt0 + s) * 128);
+      for (int j = 0; j < nk; ++j) {
+        const int st = j % kT2Stages;
+        if (!mbar_wait(&kv_empty[st], ((j / kT2Stages) & 1) ^ 1u, abort_flag, a.status)) break;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
+        uint8_t* kv = smem + kT2OffKV + st * 2 * kTile;
+        tma_load_3d(kv, &tm, &kv_full[st], 512 + head * 64, band, j * 128);
+        tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, j * 128);
+      }
+    }
+  } else if (warp == kT2WarpMma) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16_f32(128, 128);
+      const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
+      auto issue_s = [&](int s, int st) {
+        const uint32_t sq = smem_u32(smem + kT2OffQ + s * kTile);
+        const uint32_t sk = smem_u32(smem + kT2OffKV + st * 2 * kTile);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f16_ss(tmem + t2_col_s(s), sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
+                     k > 0 ? 1u : 0u);
+      };
+      auto issue_pv = [&](int s, int st, bool acc) {
+        const uint32_t sv = smem_u32(smem + kT2OffKV + (st * 2 + 1) * kTile);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + t2_col_o(s), tmem + t2_col_p(s) + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
+                     (acc || kk > 0) ? 1u : 0u);
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag, a.status);
+      if (ok) {
+        tc_fence_after();
+        for (int s = 0; s < nslots; ++s) {
+          issue_s(s, 0);
+          mma_commit(&s_full[s]);
+        }
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        const int st = j % kT2Stages;
+        // S_s(j+1) as soon as slot s holds S_s(j) in registers: it overlaps
+        // the whole softmax of tile j
+        if (j + 1 < nk) {
+          const int st1 = (j + 1) % kT2Stages;
+          ok = mbar_wait(&kv_full[st1], ((j + 1) / kT2Stages) & 1, abort_flag, a.status);
+          for (int s = 0; ok && s < nslots; ++s) {
+            ok = mbar_wait(&s_free[s], j & 1, abort_flag, a.status);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(s, st1);
+            mma_commit(&s_full[s]);
+          }
+        }
+        for (int s = 0; ok && s < nslots; ++s) {
+          ok = mbar_wait(&p_full[s], j & 1, abort_flag, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(s, st, j > 0);
+          mma_commit(&o_done[s]);
+        }
+        if (ok) mma_commit(&kv_empty[st]);
+      }
+    }
+  } else if (warp < 8) {
+    // ---------------- softmax + epilogue (one query row per thread) ----------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kT2RegsSoftmax));
+    const int slot = warp >> 2;
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t2_col_s(slot);
+    const uint32_t tO = tmem + lane_off + t2_col_o(slot);
+    const uint32_t tP = tmem + lane_off + t2_col_p(slot);
+    const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = slot < nslots;
+    for (int j = 0; ok && j < nk; ++j) {
+      ok = mbar_wait(&s_full[slot], j & 1, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      const int hi = min(128, T - j * 128);  // valid keys of this tile: [0, hi)
+      uint32_t s[4][32];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(tS + q4 * 32, s[q4]);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld_wait(s[q4]);
+      // S is in registers: the MMA warp may overwrite it with the next tile
+      tc_fence_before();
+      mbar_arrive(&s_free[slot]);
+      if (hi < 128) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (q4 * 32 + k >= hi) s[q4][k] = __float_as_uint(-INFINITY);
+      }
+      // row max: eight independent chains of three-input max, then a tree
+      float mq[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t* v = &s[c >> 1][(c & 1) * 16];
+        float m = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
+#pragma unroll
+        for (int k = 3; k < 15; k += 2) m = max3f(m, __uint_as_float(v[k]), __uint_as_float(v[k + 1]));
+        mq[c] = fmaxf(m, __uint_as_float(v[15]));
+      }
+      const float mx = max3f(max3f(mq[0], mq[1], mq[2]), max3f(mq[3], mq[4], mq[5]), fmaxf(mq[6], mq[7]));
+      const float m_new = fmaxf(m_run, mx);
+      // Keep the running reference max unless the row max grew by more than
+      // 2^8 in exp2 units (exponents stay <= 2^8 in fp32 and in the fp16 P),
+      // so O needs no rescale on most tiles.
+      float m_use, corr, m_next;
+      if (m_run == -INFINITY || (m_new - m_run) * sc > 8.0f) {
+        m_use = m_new == -INFINITY ? 0.f : m_new;
+        corr = ex2((m_run - m_use) * sc);
+        m_next = m_new;
+      } else {
+        m_use = m_run;
+        corr = 1.0f;
+        m_next = m_run;
+      }
+      const float msc = m_use * sc;
+      uint32_t w[64];
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(s[q4][2 * k]), __uint_as_float(s[q4][2 * k + 1])),
+                                       make_float2(sc, sc), make_float2(-msc, -msc));
+          const float2 p = make_float2(ex2(a2.x), ex2(a2.y));
+          sum2[k & 3] = __fadd2_rn(sum2[k & 3], p);
+          w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
+        }
+      }
+      const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
+      const float sum = sa.x + sa.y;
+      if (j > 0) {
+        // O_s += P V_{j-1} must be complete before O is rescaled and P rewritten
+        ok = mbar_wait(&o_done[slot], (j - 1) & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
+#pragma unroll 1
+          for (int c = 0; c < 64; c += 32) {
+            uint32_t v[32];
+            tmem_ld32(tO + c, v);
+            tmem_ld_wait(v);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const float2 o = __fmul2_rn(make_float2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1])),
+                                          make_float2(corr, corr));
+              v[2 * k] = __float_as_uint(o.x);
+              v[2 * k + 1] = __float_as_uint(o.y);
+            }
+            tmem_st32(tO + c, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(w));
+      tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(w + 32));
+      tmem_st_wait();
+      l_run = l_run * corr + sum;
+      m_run = m_next;
+      tc_fence_before();
+      mbar_arrive(&p_full[slot]);
+    }
+    if (ok) ok = mbar_wait(&o_done[slot], (nk - 1) & 1, abort_flag, a.status);
+    tc_fence_after();
+    if (ok && !*abort_flag) {
+      const int qi = (qt0 + slot) * 128 + r;
+      const bool valid = qi < T;
+      const int token = qi * nb + band;
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      float sig = 0.f;
+      if (valid) sig = 1.0f / (1.0f + __expf(-__ldg(a.gates + static_cast<size_t>(token) * 8 + head)));
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tO + c, v);
+        tmem_ld_wait(v);
+        if (!valid) continue;
+        uint32_t o16[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float o0 = f16_round(__uint_as_float(v[2 * k]) * inv);
+          const float o1 = f16_round(__uint_as_float(v[2 * k + 1]) * inv);
+          o16[k] = pack_f16x2(o0 * sig, o1 * sig);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(token) * 512 + head * 64 + c);
+        dst[0] = make_uint4(o16[0], o16[1], o16[2], o16[3]);
+        dst[1] = make_uint4(o16[4], o16[5], o16[6], o16[7]);
+        dst[2] = make_uint4(o16[8], o16[9], o16[10], o16[11]);
+        dst[3] = make_uint4(o16[12], o16[13], o16[14], o16[15]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kT2WarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kT2TmemCols);
+  }
+}
 }  // namespace
 
 cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
@@ -324,7 +620,15 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
     if (e != cudaSuccess) return e;
+    // setmaxnreg.inc waits until the block's launch registers cover the split;
+    // refuse to launch a build whose register count would not
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, attn_time_kernel);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs * kT2Threads < 2 * 128 * kT2RegsSoftmax + 128 * kT2RegsOther) return cudaErrorInvalidConfiguration;
     configured = true;
   }
   if (T <= 0) return cudaSuccess;
@@ -341,8 +645,11 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   dim3 grid;
   if (axis == 0) {
     e = make_map_3d(&tm, qkv, 1536, nb, T, 1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
+    if (e != cudaSuccess) return e;
     a.nk = (T + 127) / 128;
-    grid = dim3((T + 127) / 128, nb * 8);
+    // two query tiles per CTA
+    attn_time_kernel<<<dim3((a.nk + 1) / 2, nb * 8), kT2Threads, kT2Smem, st>>>(tm, a);
+    return cudaGetLastError();
   } else {
     e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
     a.nk = 1;

@@ -64,6 +64,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete is
+// suspended (issuing nothing) until the phase completes or about `ns`
+// nanoseconds pass, so waiting warps leave the issue slots to the warps that
+// compute.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t kSuspendHintNs = 1000000u;  // 1 ms per suspension; the phase completing ends it early
+
 // Wait for the phase with the given parity.  Returns false (and raises the
 // CTA-wide abort flag and the device status) when the time limit passes or
 // another thread of the CTA already gave up.
@@ -71,15 +88,13 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
-        *abort_flag = 1;
-        report_status(status, kDevWaitTimeout);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      *abort_flag = 1;
+      report_status(status, kDevWaitTimeout);
+      return false;
     }
   }
 }
