@@ -321,20 +321,21 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
 // Time axis: two query tiles per CTA, ping-pong between tensor core and softmax
 // ---------------------------------------------------------------------------
 // One CTA (1 per SM, 384 threads) owns query tiles 2x and 2x+1 of one
-// (band, head) sequence; they share every K/V tile (3-stage TMA ring).  TMEM
+// (band, head) sequence; they share every K/V tile (4-stage TMA ring).  TMEM
 // (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383, P0
 // 384..447, P1 448..511.  Warpgroup 0 (warps 0..3) runs the softmax of slot
 // 0, warpgroup 1 (warps 4..7) that of slot 1, one query row per thread (warp
-// w reads TMEM lanes 32*(w%4)..); in warpgroup 2 warp 8 loads and warp 9
-// issues the MMAs.  As soon as slot s holds S_s(j) in registers the MMA warp
-// computes S_s(j+1) into the same columns, and once P_s(j) is written,
-// O_s += P_s V_j, so the tensor core works while both softmaxes run.  The
-// softmax warpgroups take 224 registers per thread from warpgroup 2
-// (setmaxnreg), enough for a whole S row and its fp16 P without spilling.
+// w reads TMEM lanes 32*(w%4)..); in warpgroup 2 warp 8 loads and warps 9
+// and 10 issue the MMAs of slots 0 and 1.  When slot s has written P_s(j), its
+// MMA warp issues O_s += P_s V_j and then S_s(j+2) into the S columns the
+// softmax has already read (S runs two key tiles ahead), so the softmax never
+// waits for its S.  The softmax warpgroups take 224 registers per thread from
+// warpgroup 2 (setmaxnreg), enough for a whole S row and its fp16 P without
+// spilling.
 constexpr int kT2Threads = 384;
-constexpr int kT2WarpTma = 8, kT2WarpMma = 9;
+constexpr int kT2WarpTma = 8, kT2WarpMma = 9;  // warps 9 and 10 issue the MMAs of slots 0 and 1
 constexpr int kT2RegsSoftmax = 224, kT2RegsOther = 48;
-constexpr int kT2Stages = 3;
+constexpr int kT2Stages = 4;
 constexpr int kT2OffQ = 0;
 constexpr int kT2OffKV = 2 * kTile;  // stage st: K at +2*st*kTile, V at +(2*st+1)*kTile
 constexpr int kT2OffBar = kT2OffKV + kT2Stages * 2 * kTile;
@@ -357,10 +358,9 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2OffBar);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;    // [kT2Stages]
-  uint64_t* kv_empty = bars + 4;   // [kT2Stages]
-  uint64_t* s_full = bars + 7;     // [2]
-  uint64_t* p_full = bars + 9;     // [2]
-  uint64_t* o_done = bars + 11;    // [2]
+  uint64_t* kv_empty = bars + 5;   // [kT2Stages]
+  uint64_t* s_full = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;    // [2]
   uint64_t* s_free = bars + 13;    // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -378,12 +378,11 @@ __global__ void __launch_bounds__(kT2Threads, 1)
     mbar_init(q_full, 1);
     for (int i = 0; i < kT2Stages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&kv_empty[i], nslots);  // one commit per slot's MMA issuer
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
-      mbar_init(&o_done[i], 1);
       mbar_init(&s_free[i], 128);
     }
     *abort_flag = 0;
@@ -417,20 +416,26 @@ __global__ void __launch_bounds__(kT2Threads, 1)
         tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, j * 128);
       }
     }
-  } else if (warp == kT2WarpMma) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+  } else if (warp == kT2WarpMma || warp == kT2WarpMma + 1) {
+    // ---------------- MMA issuers, one per slot ----------------
+    // tcgen05.mma issue blocks while the tensor pipe is busy, so each slot has
+    // its own issuing thread: one slot's waits overlap the other's MMAs.
+    // s_full[s] completes phase 0 with S_s(0), phase 1 with S_s(1), and phase
+    // j+2 with O_s += P_s(j) V_j together with S_s(j+2): S runs two key tiles
+    // ahead of the softmax, PV one behind.
+    const int s = warp - kT2WarpMma;
+    if (lane == 0 && s < nslots) {
       const uint32_t id_s = idesc_f16_f32(128, 128);
       const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
-      auto issue_s = [&](int s, int st) {
-        const uint32_t sq = smem_u32(smem + kT2OffQ + s * kTile);
+      const uint32_t sq = smem_u32(smem + kT2OffQ + s * kTile);
+      auto issue_s = [&](int st) {
         const uint32_t sk = smem_u32(smem + kT2OffKV + st * 2 * kTile);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_f16_ss(tmem + t2_col_s(s), sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
                      k > 0 ? 1u : 0u);
       };
-      auto issue_pv = [&](int s, int st, bool acc) {
+      auto issue_pv = [&](int st, bool acc) {
         const uint32_t sv = smem_u32(smem + kT2OffKV + (st * 2 + 1) * kTile);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
@@ -441,34 +446,33 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag, a.status);
       if (ok) {
         tc_fence_after();
-        for (int s = 0; s < nslots; ++s) {
-          issue_s(s, 0);
-          mma_commit(&s_full[s]);
-        }
-      }
-      for (int j = 0; ok && j < nk; ++j) {
-        const int st = j % kT2Stages;
-        // S_s(j+1) as soon as slot s holds S_s(j) in registers: it overlaps
-        // the whole softmax of tile j
-        if (j + 1 < nk) {
-          const int st1 = (j + 1) % kT2Stages;
-          ok = mbar_wait(&kv_full[st1], ((j + 1) / kT2Stages) & 1, abort_flag, a.status);
-          for (int s = 0; ok && s < nslots; ++s) {
-            ok = mbar_wait(&s_free[s], j & 1, abort_flag, a.status);
-            if (!ok) break;
+        issue_s(0);
+        mma_commit(&s_full[s]);
+        if (nk > 1) {
+          ok = mbar_wait(&kv_full[1], 0, abort_flag, a.status);
+          if (ok) ok = mbar_wait(&s_free[s], 0, abort_flag, a.status);
+          if (ok) {
             tc_fence_after();
-            issue_s(s, st1);
-            mma_commit(&s_full[s]);
+            issue_s(1);
           }
         }
-        for (int s = 0; ok && s < nslots; ++s) {
-          ok = mbar_wait(&p_full[s], j & 1, abort_flag, a.status);
+        if (ok) mma_commit(&s_full[s]);
+      }
+      for (int j = 0; ok && j < nk; ++j) {
+        ok = mbar_wait(&p_full[s], j & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(j % kT2Stages, j > 0);
+        if (j + 2 < nk) {
+          const int st2 = (j + 2) % kT2Stages;
+          ok = mbar_wait(&kv_full[st2], ((j + 2) / kT2Stages) & 1, abort_flag, a.status);
+          if (ok) ok = mbar_wait(&s_free[s], (j + 1) & 1, abort_flag, a.status);
           if (!ok) break;
           tc_fence_after();
-          issue_pv(s, st, j > 0);
-          mma_commit(&o_done[s]);
+          issue_s(st2);
         }
-        if (ok) mma_commit(&kv_empty[st]);
+        mma_commit(&s_full[s]);
+        mma_commit(&kv_empty[j % kT2Stages]);
       }
     }
   } else if (warp < 8) {
@@ -546,8 +550,9 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
       const float sum = sa.x + sa.y;
       if (j > 0) {
-        // O_s += P V_{j-1} must be complete before O is rescaled and P rewritten
-        ok = mbar_wait(&o_done[slot], (j - 1) & 1, abort_flag, a.status);
+        // O_s += P V_{j-1} (phase j+1) must be complete before O is rescaled
+        // and P rewritten
+        ok = mbar_wait(&s_full[slot], (j + 1) & 1, abort_flag, a.status);
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, corr != 1.0f)) {
@@ -576,7 +581,10 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       tc_fence_before();
       mbar_arrive(&p_full[slot]);
     }
-    if (ok) ok = mbar_wait(&o_done[slot], (nk - 1) & 1, abort_flag, a.status);
+    // last PV: phase nk+1 (with a single key tile, phase 1 is passed first so
+    // that the parity wait never runs two phases behind)
+    if (ok && nk == 1) ok = mbar_wait(&s_full[slot], 1, abort_flag, a.status);
+    if (ok) ok = mbar_wait(&s_full[slot], (nk + 1) & 1, abort_flag, a.status);
     tc_fence_after();
     if (ok && !*abort_flag) {
       const int qi = (qt0 + slot) * 128 + r;
