@@ -17,6 +17,7 @@
 // rescale O in TMEM, and finally write f16(f16(O/l) * sigmoid(gate)).  Keeping
 // P in TMEM halves the shared-memory traffic of a key tile.
 #include "common.cuh"
+#include "exp2_poly.cuh"
 #include "kernels.h"
 
 namespace lbrr {
@@ -363,6 +364,7 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   uint64_t* p_full = bars + 11;    // [2]
   uint64_t* s_free = bars + 13;    // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* turn = bars + 16;      // [2] exponentials: slot 0 and slot 1 take turns
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -384,6 +386,7 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&s_free[i], 128);
+      mbar_init(&turn[i], 4);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -488,6 +491,15 @@ __global__ void __launch_bounds__(kT2Threads, 1)
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = slot < nslots;
+    // The exponentials of a key tile (one MUFU ex2 per score, the SM's
+    // narrowest pipe) alternate strictly between the slots: slot 0 tile j,
+    // slot 1 tile j, slot 0 tile j+1, ...  Each then runs alone on the pipe
+    // while the other slot loads S, takes the row max and stores P.
+    const bool take_turns = nslots == 2;
+    if (ok && take_turns && slot == 1) {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&turn[0]);  // slot 0 goes first
+    }
     for (int j = 0; ok && j < nk; ++j) {
       ok = mbar_wait(&s_full[slot], j & 1, abort_flag, a.status);
       if (!ok) break;
@@ -534,6 +546,10 @@ __global__ void __launch_bounds__(kT2Threads, 1)
         m_next = m_run;
       }
       const float msc = m_use * sc;
+      if (take_turns) {
+        ok = mbar_wait(&turn[slot], j & 1, abort_flag, a.status);
+        if (!ok) break;
+      }
       uint32_t w[64];
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -542,10 +558,15 @@ __global__ void __launch_bounds__(kT2Threads, 1)
         for (int k = 0; k < 16; ++k) {
           const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(s[q4][2 * k]), __uint_as_float(s[q4][2 * k + 1])),
                                        make_float2(sc, sc), make_float2(-msc, -msc));
-          const float2 p = make_float2(ex2(a2.x), ex2(a2.y));
+          // 5 of every 16 pairs on the FMA pipe, the rest on MUFU
+          const float2 p = k >= 11 ? exp2_poly2(a2) : make_float2(ex2(a2.x), ex2(a2.y));
           sum2[k & 3] = __fadd2_rn(sum2[k & 3], p);
           w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
         }
+      }
+      if (take_turns) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&turn[slot ^ 1]);
       }
       const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
       const float sum = sa.x + sa.y;

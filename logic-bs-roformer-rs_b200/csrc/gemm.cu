@@ -26,7 +26,7 @@ namespace lbrr {
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kBN = 256;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 constexpr int kABytes = kBM * kBK * 2;          // 16 KB
 constexpr int kBBytes = kBN * kBK * 2;          // 32 KB
 constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
@@ -35,20 +35,48 @@ constexpr int kParts = kEpiWarps / 4;           // epilogue warps per TMEM lane 
 constexpr int kPartCols = kBN / kParts;         // accumulator columns per epilogue warp
 constexpr int kStageWords = 32 * 32;            // per-warp staging buffer (4 KB)
 constexpr int kStagingOff = kStages * kStageBytes;
-constexpr int kBarOff = kStagingOff + kEpiWarps * kStageWords * 4;
+// per-CTA copy of the epilogue's constant vectors (bias, gamma, gate weights,
+// RoPE tables), loaded once when the kernel starts; read with shared-memory
+// broadcasts instead of per-block global loads
+constexpr int kConstFloats = 6144;
+constexpr int kConstOff = kStagingOff + kEpiWarps * kStageWords * 4;
+constexpr int kBarOff = kConstOff + kConstFloats * 4;
 constexpr int kGemmSmem = kBarOff + 256;
 constexpr int kGemmThreads = 64 + kEpiWarps * 32;
 constexpr uint32_t kTmemCols = 512;
 static_assert(kGemmSmem <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
 
 // ---------------------------------------------------------------------------
+// Division by a launch constant: q = umulhi(x, m), m = ceil(2^32 / d), which is
+// exact for x * d < 2^32 (|error| of x*m/2^32 - x/d stays below 1/d); the host
+// leaves m = 0, meaning a plain division, when that bound does not hold.
+// ---------------------------------------------------------------------------
+struct FastDiv {
+  uint32_t d = 1, m = 0;
+  __device__ __forceinline__ int div(int x) const {
+    const uint32_t u = static_cast<uint32_t>(x);
+    return static_cast<int>(m ? __umulhi(u, m) : (d == 1 ? u : u / d));
+  }
+};
+static inline FastDiv make_fastdiv(uint32_t d, uint64_t x_max) {
+  FastDiv f;
+  f.d = d;
+  if (d > 1 && x_max * d < (1ull << 32)) f.m = static_cast<uint32_t>(((1ull << 32) + d - 1) / d);
+  return f;
+}
+
+// ---------------------------------------------------------------------------
 // Tile resolvers
 // ---------------------------------------------------------------------------
+struct EpiCtx;
 struct DenseTiles {
   int M, n_tiles, kblocks;
+  FastDiv ntd;  // division by n_tiles
+  __device__ void load_consts(float*, int, int) const {}
+  __device__ void prefetch(const TileDesc&, EpiCtx&) const {}
   __device__ TileDesc tile(int idx) const {
     TileDesc t;
-    const int mt = idx / n_tiles, nt = idx % n_tiles;
+    const int mt = ntd.div(idx), nt = idx - mt * n_tiles;
     t.a_row = mt * kBM;
     t.a_col = 0;
     t.b_row = nt * kBN;
@@ -62,6 +90,8 @@ struct DenseTiles {
 };
 struct TableTiles {
   const TileDesc* table;
+  __device__ void load_consts(float*, int, int) const {}
+  __device__ void prefetch(const TileDesc&, EpiCtx&) const {}
   __device__ TileDesc tile(int idx) const { return table[idx]; }
 };
 
@@ -110,6 +140,10 @@ struct EpiCtx {
   Stager st;        // this warp's staging buffer
   uint32_t* quad;   // staging buffers of the kParts warps sharing these rows (part-major)
   int bar_id;       // named barrier shared by those warps
+  float* consts;    // the epilogue's constants in shared memory (load_consts)
+  int id;           // epilogue warp index 0..kEpiWarps-1 (part * 4 + q)
+  int next_tile;    // index of this CTA's next tile, or -1
+  float4 pre;       // epilogue data for the next tile, fetched during this one (Epi::prefetch)
 };
 
 // Write this lane's row (W = 16 words: 32 fp16, W = 32: 32 fp32) into buf.
@@ -182,6 +216,37 @@ __device__ __forceinline__ void quad_sync(int id) {
 }
 
 __device__ __forceinline__ float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+// 16-byte shared-memory load (p points into the constants region)
+__device__ __forceinline__ float4 lds4(const float* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(smem_u32(p)));
+  return v;
+}
+// Copy n floats (n a multiple of 4, 16-byte aligned) into shared memory with the epilogue threads.
+__device__ __forceinline__ void copy_consts(float* dst, const float* src, int n, int tid, int nthr) {
+  for (int i = 4 * tid; i < n; i += 4 * nthr)
+    *reinterpret_cast<float4*>(dst + i) = __ldg(reinterpret_cast<const float4*>(src + i));
+}
+// Run body(v, c) over this warp's kPartCols accumulator columns in blocks of
+// 32, the TMEM load of block b+1 in flight while block b is processed.
+template <class Body>
+__device__ __forceinline__ void for_each_block(const EpiCtx& x, Body body) {
+  static_assert(kPartCols % 64 == 0, "blocks are processed in pairs");
+  uint32_t va[32], vb[32];
+  tmem_ld32(x.tm + x.c0, va);
+  tmem_ld_wait(va);
+#pragma unroll
+  for (int b = 0; b < kPartCols / 32; b += 2) {
+    tmem_ld32(x.tm + x.c0 + 32 * (b + 1), vb);
+    body(va, x.c0 + 32 * b);
+    tmem_ld_wait(vb);
+    if (b + 2 < kPartCols / 32) tmem_ld32(x.tm + x.c0 + 32 * (b + 2), va);
+    body(vb, x.c0 + 32 * (b + 1));
+    if (b + 2 < kPartCols / 32) tmem_ld_wait(va);
+  }
+}
 
 __device__ __forceinline__ float rcp_approx(float x) {
   float y;
@@ -243,26 +308,83 @@ struct EpiQKV : DenseTiles {
   const float* cos;     // [P][32]
   const float* sin;
   int nb, axis;
+  // constants: bias [0, 1536); RoPE rows from kRope as [pos][cos 32 | sin 32]:
+  // frequency axis the whole table (nb <= kMaxNb positions), time axis a
+  // per-warp cache of the (at most two) frames its 32 rows fall in
+  static constexpr int kRope = 1536;
+  static constexpr int kMaxNb = (kConstFloats - kRope) / 64;
+  __device__ void load_consts(float* c, int tid, int nthr) const {
+    copy_consts(c, bias16, 1536, tid, nthr);
+    if (axis == 1 && nb <= kMaxNb)
+      for (int i = tid; i < nb * 64; i += nthr) {
+        const int pos = i >> 6, k = i & 63;
+        c[kRope + i] = k < 32 ? __ldg(cos + pos * 32 + k) : __ldg(sin + pos * 32 + k - 32);
+      }
+  }
+  FastDiv nbd;  // division by nb
+  // Time axis: first frame and number of frames of the 32 rows of quadrant q.
+  __device__ bool frames_of(const TileDesc& t, int q, int& p_lo, int& span) const {
+    const int r_lo = t.row0 + q * 32;
+    const int r_hi = min(r_lo + 31, t.row0 + t.rows - 1);
+    if (r_lo > r_hi) return false;
+    p_lo = nbd.div(r_lo);
+    span = nbd.div(r_hi) - p_lo + 1;
+    return true;
+  }
+  // Time axis: lane l's four floats of the cache rows p_lo, p_lo+1 of tile t
+  // (row l/16, cos|sin column 4*(l%16)), fetched one tile ahead: a global load
+  // in the middle of the GEMM's stores takes about a microsecond.
+  __device__ void prefetch(const TileDesc& t, EpiCtx& x) const {
+    int p_lo, span;
+    x.pre = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (axis != 0 || !frames_of(t, x.q, p_lo, span) || span > 2) return;
+    const int row = x.lane >> 4, k4 = (x.lane & 15) * 4;
+    if (row < span) x.pre = ldg4((k4 < 32 ? cos + k4 : sin + (k4 - 32)) + (p_lo + row) * 32);
+  }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int r = t.row0 + x.row;
     const bool valid = x.row < t.rows;
-    const int pos = valid ? (axis == 0 ? r / nb : r % nb) : 0;
-#pragma unroll 1
-    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(x.tm + c, v);
-      tmem_ld_wait(v);
+    const int pq = nbd.div(r);
+    const int pos = valid ? (axis == 0 ? pq : r - pq * nb) : 0;
+    // this thread's RoPE row: cos at rope[0..31], sin at rope[32..63]
+    const float* rope = nullptr;
+    bool rope_smem = false;
+    if (axis == 1) {
+      if (nb <= kMaxNb) {
+        rope = x.consts + kRope + pos * 64;
+        rope_smem = true;
+      }
+    } else {
+      int p_lo, span;
+      if (frames_of(t, x.q, p_lo, span) && span <= 2) {
+        float* cache = x.consts + kRope + x.id * 128;
+        __syncwarp();  // the previous tile's reads of the cache are done
+        const int row = x.lane >> 4, k4 = (x.lane & 15) * 4;
+        if (row < span) *reinterpret_cast<float4*>(cache + row * 64 + k4) = x.pre;
+        __syncwarp();
+        // rows past the end of the matrix (pos 0) read a valid cache row
+        rope = cache + (valid ? pos - p_lo : 0) * 64;
+        rope_smem = true;
+      }
+      if (x.next_tile >= 0) prefetch(tile(x.next_tile), x);
+    }
+    for_each_block(x, [&](uint32_t(&v)[32], int c) {
       const int col = t.aux + c;
       const bool rot = col < 1024;
       const int pair0 = (col & 63) >> 1;
       uint32_t w[16];
 #pragma unroll
       for (int j4 = 0; j4 < 4; ++j4) {
-        const float4 b0 = ldg4(bias16 + col + 8 * j4), b1 = ldg4(bias16 + col + 8 * j4 + 4);
+        const float4 b0 = lds4(x.consts + col + 8 * j4), b1 = lds4(x.consts + col + 8 * j4 + 4);
         float4 cs = make_float4(1.f, 1.f, 1.f, 1.f), sn = make_float4(0.f, 0.f, 0.f, 0.f);
         if (rot) {
-          cs = ldg4(cos + pos * 32 + pair0 + 4 * j4);
-          sn = ldg4(sin + pos * 32 + pair0 + 4 * j4);
+          if (rope_smem) {
+            cs = lds4(rope + pair0 + 4 * j4);
+            sn = lds4(rope + 32 + pair0 + 4 * j4);
+          } else {
+            cs = ldg4(cos + pos * 32 + pair0 + 4 * j4);
+            sn = ldg4(sin + pos * 32 + pair0 + 4 * j4);
+          }
         }
         const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
         const float cc[4] = {cs.x, cs.y, cs.z, cs.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
@@ -273,9 +395,7 @@ struct EpiQKV : DenseTiles {
           if (rot) {
             // (e c - o s, o c + e s), products rounded separately like the
             // reference's rope kernels, applied to the fp32 pair and rounded to
-            // fp16 once (the reference rounds before and after the rotation;
-            // one fp16 conversion per pair instead of two keeps the XU pipe,
-            // which executes the conversions, off the critical path)
+            // fp16 once (the reference rounds before and after the rotation)
             const float2 p1 = __fmul2_rn(eo, f2(cc[j], cc[j]));
             const float2 p2 = __fmul2_rn(f2(eo.y, eo.x), f2(-ss[j], ss[j]));
             const float2 o2 = __fadd2_rn(p1, p2);
@@ -288,25 +408,23 @@ struct EpiQKV : DenseTiles {
       uint32_t* buf = x.st.f16_buf();
       stage_row<16>(buf, w, x.lane);
       store_2d(&out_map, buf, col, t.row0 + x.q * 32, x.lane);
-    }
+    });
   }
 };
 
 // FF1: f16(gelu_AS(acc + b1)) (gemm_f16_gelu_a16w epilogue, src/main.rs:2918-2948).
 struct EpiGelu : DenseTiles {
   CUtensorMap out_map;  // ff1 [M][1024] fp16, box 32 x 32, 64-byte swizzle
-  const float* bias;    // [N]
+  const float* bias;    // [N <= kConstFloats]
+  int n;
+  __device__ void load_consts(float* c, int tid, int nthr) const { copy_consts(c, bias, n, tid, nthr); }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
-#pragma unroll 1
-    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(x.tm + c, v);
-      tmem_ld_wait(v);
+    for_each_block(x, [&](uint32_t(&v)[32], int c) {
       const int col = t.aux + c;
       uint32_t w[16];
 #pragma unroll
       for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 b = ldg4(bias + col + 4 * j4);
+        const float4 b = lds4(x.consts + col + 4 * j4);
         const float2 g0 = gelu_as2(__fadd2_rn(f2(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1])), f2(b.x, b.y)));
         const float2 g1 =
             gelu_as2(__fadd2_rn(f2(__uint_as_float(v[4 * j4 + 2]), __uint_as_float(v[4 * j4 + 3])), f2(b.z, b.w)));
@@ -316,7 +434,7 @@ struct EpiGelu : DenseTiles {
       uint32_t* buf = x.st.f16_buf();
       stage_row<16>(buf, w, x.lane);
       store_2d(&out_map, buf, col, t.row0 + x.q * 32, x.lane);
-    }
+    });
   }
 };
 
@@ -345,10 +463,20 @@ struct Row256Maps {
   CUtensorMap h16_map;  // fp16 rows (norm 1, 2), box 32 x 32 (x 1), 64-byte swizzle
 };
 
-template <bool kBandRows, class RowOf>
+// Constants of the dense row epilogue in shared memory (EpiRow256::load_consts).
+constexpr int kRowBias = 0, kRowGamma = 256, kRowGateW = 512, kRowGateB = 512 + 2048;
+
+// kSmem: bias, gamma, gate_w and gate_b are read from the constants region
+// (x.consts, layout above) instead of global memory.
+template <bool kBandRows, bool kSmem, class RowOf>
 __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, const float* bias, const float* resid,
                                                 const Row256Maps& maps, const RowNormParams& np, int band,
                                                 RowOf row_of) {
+  auto ld4 = [](const float* p) { return kSmem ? lds4(p) : ldg4(p); };
+  const float* gamma = kSmem ? x.consts + kRowGamma : np.gamma;
+  const float* gate_w = kSmem ? x.consts + kRowGateW : np.gate_w;
+  const float* gate_b = kSmem ? x.consts + kRowGateB : np.gate_b;
+  if (kSmem) bias = x.consts + kRowBias;
   const bool valid = x.row < t.rows;
   const int my_row = valid ? row_of(x.row) : 0;  // global token row of this thread
   const int rb = x.q * 32;
@@ -378,7 +506,7 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
     tmem_ld_wait(v);
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
-      const float4 b = ldg4(bias + c + 4 * j4);
+      const float4 b = ld4(bias + c + 4 * j4);
       const float2 o01 = __fadd2_rn(__fadd2_rn(f2(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1])), f2(b.x, b.y)),
                                     f2(rr[j4].x, rr[j4].y));
       const float2 o23 =
@@ -418,7 +546,7 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
     uint32_t w[16];
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
-      const float4 gm = ldg4(np.gamma + c + 4 * j4);
+      const float4 gm = ld4(gamma + c + 4 * j4);
       const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
       float h[4];
 #pragma unroll
@@ -429,7 +557,7 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
       if (np.norm == 2) {
 #pragma unroll
         for (int gi = 0; gi < 8; ++gi) {
-          const float4 wg = ldg4(np.gate_w + gi * 256 + c + 4 * j4);
+          const float4 wg = ld4(gate_w + gi * 256 + c + 4 * j4);
           g[gi] += h[0] * wg.x + h[1] * wg.y + h[2] * wg.z + h[3] * wg.w;
         }
       }
@@ -457,7 +585,7 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
       float tot[8];
 #pragma unroll
       for (int gi = 0; gi < 8; ++gi) {
-        tot[gi] = __ldg(np.gate_b + gi);
+        tot[gi] = kSmem ? gate_b[gi] : __ldg(gate_b + gi);
 #pragma unroll
         for (int p = 0; p < kParts; ++p) tot[gi] += __uint_as_float(x.quad[p * kStageWords + gi * 32 + x.lane]);
       }
@@ -479,8 +607,16 @@ struct EpiRow256 : DenseTiles {
   const float* bias;
   const float* resid;
   RowNormParams np;
+  __device__ void load_consts(float* c, int tid, int nthr) const {
+    copy_consts(c + kRowBias, bias, 256, tid, nthr);
+    if (np.norm) copy_consts(c + kRowGamma, np.gamma, 256, tid, nthr);
+    if (np.norm == 2) {
+      copy_consts(c + kRowGateW, np.gate_w, 2048, tid, nthr);
+      if (tid < 8) c[kRowGateB + tid] = __ldg(np.gate_b + tid);
+    }
+  }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
-    row256_epilogue<false>(t, x, bias, resid, maps, np, 0, [&](int r) { return t.row0 + r; });
+    row256_epilogue<false, true>(t, x, bias, resid, maps, np, 0, [&](int r) { return t.row0 + r; });
   }
 };
 
@@ -493,7 +629,7 @@ struct EpiBand : TableTiles {
   RowNormParams np;
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int band = t.aux;
-    row256_epilogue<true>(t, x, bias + band * 256, nullptr, maps, np, band,
+    row256_epilogue<true, false>(t, x, bias + band * 256, nullptr, maps, np, band,
                           [&](int r) { return (t.row0 + r) * nb + band; });
   }
 };
@@ -694,6 +830,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     x.st.phase = 0;
     x.st.last_f32 = false;
     x.bar_id = 1 + x.q;
+    float* consts = reinterpret_cast<float*>(smem + kConstOff);
+    x.consts = consts;
+    x.id = x.part * 4 + x.q;
+    if (static_cast<int>(blockIdx.x) < n_tiles) epi.prefetch(epi.tile(blockIdx.x), x);
+    epi.load_consts(consts, ew * 32 + lane, kEpiWarps * 32);
+    // all epilogue warps, once, before any tile: the constants are complete
+    asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
     int i = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
       const TileDesc t = epi.tile(tile);
@@ -701,6 +844,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!mbar_wait(&acc_full[slot], (i >> 1) & 1, abort_flag, status)) break;
       tc_fence_after();
       x.tm = tmem + (static_cast<uint32_t>(x.q * 32) << 16) + slot * kBN;
+      x.next_tile = tile + static_cast<int>(gridDim.x) < n_tiles ? tile + static_cast<int>(gridDim.x) : -1;
       epi.run(t, x);
       tc_fence_before();
       __syncwarp();
@@ -783,6 +927,8 @@ cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, co
   ep.M = M;
   ep.n_tiles = 1536 / kBN;
   ep.kblocks = 256 / kBK;
+  ep.ntd = make_fastdiv(ep.n_tiles, dense_tiles(M, 1536));
+  ep.nbd = make_fastdiv(static_cast<uint32_t>(nb), static_cast<uint64_t>(M));
   ep.bias16 = bias16;
   ep.cos = cos;
   ep.sin = sin;
@@ -803,6 +949,7 @@ cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const flo
   ep.M = M;
   ep.n_tiles = 1;
   ep.kblocks = 512 / kBK;
+  ep.ntd = make_fastdiv(ep.n_tiles, dense_tiles(M, 256));
   ep.bias = bias;
   ep.resid = resid;
   ep.np = RowNormParams{};
@@ -822,7 +969,9 @@ cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, 
   ep.M = M;
   ep.n_tiles = 1024 / kBN;
   ep.kblocks = 256 / kBK;
+  ep.ntd = make_fastdiv(ep.n_tiles, dense_tiles(M, 1024));
   ep.bias = b1;
+  ep.n = 1024;
   return launch_gemm(ta, tb, ep, dense_tiles(M, 1024), status, st);
 }
 
@@ -838,6 +987,7 @@ cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2,
   ep.M = M;
   ep.n_tiles = 1;
   ep.kblocks = 1024 / kBK;
+  ep.ntd = make_fastdiv(ep.n_tiles, dense_tiles(M, 256));
   ep.bias = b2;
   ep.resid = resid;
   ep.np = to_params(next);

@@ -42,21 +42,25 @@ def test_norm_gates(lb, M):
     assert rel_err(gates.cpu(), hf @ gw.T + gb) < 1e-5
 
 
-@pytest.mark.parametrize("T,axis", [(1, 0), (37, 0), (259, 0), (1, 1), (37, 1)])
-def test_qkv_rope(lb, T, axis):
-    M = T * NB
+# (1151, 62): the full chunk, whose last tile has rows past the end; bands 1
+# and 100 take the epilogue's global-memory RoPE path (a 32-row warp spans more
+# than two frames / the table exceeds the shared-memory copy)
+@pytest.mark.parametrize("T,axis,nb", [(1, 0, NB), (37, 0, NB), (259, 0, NB), (1151, 0, NB), (1, 1, NB), (37, 1, NB),
+                                       (1151, 1, NB), (300, 0, 1), (9, 1, 100)])
+def test_qkv_rope(lb, T, axis, nb):
+    M = T * nb
     h = f16(randn((M, 256), 10 + T, 1.0))
     w = f16(randn((1536, 256), 11, 0.02))
     bias16 = f16(randn((1536,), 12, 0.02))
-    P = T if axis == 0 else NB
+    P = T if axis == 0 else nb
     cos, sin = R.rope_tables(P)
     qkv = torch.empty(M, 1536, dtype=torch.float16, device="cuda")
-    lb.qkv_rope(cuda(h, torch.float16), cuda(w, torch.float16), cuda(bias16), cuda(cos), cuda(sin), qkv, T, NB, axis)
+    lb.qkv_rope(cuda(h, torch.float16), cuda(w, torch.float16), cuda(bias16), cuda(cos), cuda(sin), qkv, T, nb, axis)
     lb.op_sync()
     ref = f16(h @ w.T + bias16)
     q, k, v = ref[:, :512], ref[:, 512:1024], ref[:, 1024:]
-    qr = unfold(f16(R.rope(fold(q, T, NB, axis), cos, sin)), T, NB, axis)
-    kr = unfold(f16(R.rope(fold(k, T, NB, axis), cos, sin)), T, NB, axis)
+    qr = unfold(f16(R.rope(fold(q, T, nb, axis), cos, sin)), T, nb, axis)
+    kr = unfold(f16(R.rope(fold(k, T, nb, axis), cos, sin)), T, nb, axis)
     got = qkv.float().cpu()
     for sl, r in ((slice(0, 512), qr), (slice(512, 1024), kr), (slice(1024, 1536), v)):
         assert rel_err(got[:, sl], r) < 2e-3
