@@ -364,7 +364,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   uint64_t* p_full = bars + 11;    // [2]
   uint64_t* s_free = bars + 13;    // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
-  uint64_t* turn = bars + 16;      // [2] exponentials: slot 0 and slot 1 take turns
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -386,7 +385,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 128);
       mbar_init(&s_free[i], 128);
-      mbar_init(&turn[i], 4);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -491,15 +489,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = slot < nslots;
-    // The exponentials of a key tile (one MUFU ex2 per score, the SM's
-    // narrowest pipe) alternate strictly between the slots: slot 0 tile j,
-    // slot 1 tile j, slot 0 tile j+1, ...  Each then runs alone on the pipe
-    // while the other slot loads S, takes the row max and stores P.
-    const bool take_turns = nslots == 2;
-    if (ok && take_turns && slot == 1) {
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&turn[0]);  // slot 0 goes first
-    }
     for (int j = 0; ok && j < nk; ++j) {
       ok = mbar_wait(&s_full[slot], j & 1, abort_flag, a.status);
       if (!ok) break;
@@ -546,10 +535,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
         m_next = m_run;
       }
       const float msc = m_use * sc;
-      if (take_turns) {
-        ok = mbar_wait(&turn[slot], j & 1, abort_flag, a.status);
-        if (!ok) break;
-      }
       uint32_t w[64];
       float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
@@ -563,10 +548,6 @@ __global__ void __launch_bounds__(kT2Threads, 1)
           sum2[k & 3] = __fadd2_rn(sum2[k & 3], p);
           w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
         }
-      }
-      if (take_turns) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&turn[slot ^ 1]);
       }
       const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
       const float sum = sa.x + sa.y;
@@ -646,8 +627,8 @@ __global__ void __launch_bounds__(kT2Threads, 1)
 
 cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
                           cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
+  static unsigned long long configured = 0;
+  cudaError_t ce = once_per_device(configured, [] {
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
@@ -658,8 +639,9 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     e = cudaFuncGetAttributes(&fa, attn_time_kernel);
     if (e != cudaSuccess) return e;
     if (fa.numRegs * kT2Threads < 2 * 128 * kT2RegsSoftmax + 128 * kT2RegsOther) return cudaErrorInvalidConfiguration;
-    configured = true;
-  }
+    return cudaSuccess;
+  });
+  if (ce != cudaSuccess) return ce;
   if (T <= 0) return cudaSuccess;
   if (axis == 1 && 2 * nb > 128) return cudaErrorInvalidValue;  // two sequences per 128-row tile
   CUtensorMap tm;

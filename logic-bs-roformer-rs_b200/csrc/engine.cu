@@ -931,10 +931,17 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
     CK(cudaMemsetAsync(result, 0, static_cast<size_t>(channels) * needed * sizeof(float), e0->stream));
     CK(cudaMemsetAsync(counter, 0, static_cast<size_t>(needed) * sizeof(float), e0->stream));
   }
-  for (int i = 0; i < n; ++i) {
+  for (int i = 0; rc == LBRR_OK && i < n; ++i) {
+    // ev_done[i] is recorded on engine i's stream, ev_used[i] on the stitching
+    // stream of engine 0: an event lives on the device whose streams record it
+    {
+      DeviceGuard g0(e0->device);
+      if (cudaEventCreateWithFlags(&ev_used[i], cudaEventDisableTiming) != cudaSuccess)
+        rc = fail(LBRR_ERR_CUDA, "event create");
+    }
     DeviceGuard g(engines[i]->device);
-    cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming);
-    cudaEventCreateWithFlags(&ev_used[i], cudaEventDisableTiming);
+    if (cudaEventCreateWithFlags(&ev_done[i], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(LBRR_ERR_CUDA, "event create");
     if (i > 0 && engines[i]->device != e0->device) {
       // direct NVLink copies when peer access exists; otherwise cudaMemcpyPeerAsync
       // stages through host memory on its own
@@ -957,17 +964,17 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
       DeviceGuard g(e->device);
       // the input staging slot and dev_out of this engine are free once the
       // previous chunk's waveform was consumed by the stitching stream
-      cudaStreamWaitEvent(e->stream, ev_used[slot], 0);
+      if (cudaStreamWaitEvent(e->stream, ev_used[slot], 0) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "stream wait"); break; }
       if (cudaStreamSynchronize(e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "stream sync"); break; }
       std::memcpy(e->pin_in, xp.data() + 2 * s, static_cast<size_t>(C) * 2 * sizeof(float));
       if (cudaMemcpyAsync(e->dev_in, e->pin_in, static_cast<size_t>(C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
                           e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "H2D chunk"); break; }
       if ((rc = lbrr_forward_chunk(e, e->dev_in, C, e->dev_out, e->stream)) != LBRR_OK) break;
-      cudaEventRecord(ev_done[slot], e->stream);
+      if (cudaEventRecord(ev_done[slot], e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "event record"); break; }
     }
     {
       DeviceGuard g(e0->device);
-      cudaStreamWaitEvent(e0->stream, ev_done[slot], 0);
+      if (cudaStreamWaitEvent(e0->stream, ev_done[slot], 0) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "stream wait"); break; }
       const float* y = e->dev_out;
       if (e != e0) {
         if (cudaMemcpyPeerAsync(stage, e0->device, e->dev_out, e->device, ybytes, e0->stream) != cudaSuccess) {
@@ -980,8 +987,8 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
       ola_accumulate_kernel<<<(take + 255) / 256, 256, 0, e0->stream>>>(
           y, result, counter, needed, s, take, static_cast<int>(C), static_cast<int>(P.border), ci == 0,
           ci + 1 == starts.size(), static_cast<int>(C), channels);
-      cudaEventRecord(ev_used[slot], e0->stream);
       if (cudaGetLastError() != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "ola accumulate launch"); break; }
+      if (cudaEventRecord(ev_used[slot], e0->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "event record"); break; }
     }
   }
   if (rc == LBRR_OK) {
@@ -1007,7 +1014,12 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
     DeviceGuard g(engines[i]->device);
     cudaStreamSynchronize(engines[i]->stream);
     if (ev_done[i]) cudaEventDestroy(ev_done[i]);
-    if (ev_used[i]) cudaEventDestroy(ev_used[i]);
+  }
+  {
+    DeviceGuard g(e0->device);
+    cudaStreamSynchronize(e0->stream);
+    for (int i = 0; i < n; ++i)
+      if (ev_used[i]) cudaEventDestroy(ev_used[i]);
   }
   {
     DeviceGuard g(e0->device);

@@ -878,12 +878,11 @@ static int num_sms() {
 template <class Epi>
 static cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const Epi& epi, int tiles, int* status,
                                cudaStream_t st) {
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  static unsigned long long configured = 0;
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(gemm_tc_kernel<Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  });
+  if (e != cudaSuccess) return e;
   if (tiles <= 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
   gemm_tc_kernel<Epi><<<grid, kGemmThreads, kGemmSmem, st>>>(a, b, epi, tiles, status);

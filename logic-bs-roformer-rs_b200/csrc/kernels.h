@@ -85,4 +85,19 @@ cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, 
 cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_env, float* out, int len, int T,
                       int channels, cudaStream_t st);
 
+// cudaFuncSetAttribute (the dynamic shared-memory opt-in) acts on the current
+// device only.  Runs `setup` once per device (devices 0..63, bit d of `done`)
+// before the first launch there; a failed setup is retried on the next call.
+template <class Setup>
+inline cudaError_t once_per_device(unsigned long long& done, Setup setup) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit)) return cudaSuccess;
+  e = setup();
+  if (e == cudaSuccess && bit) __atomic_fetch_or(&done, bit, __ATOMIC_RELEASE);
+  return e;
+}
+
 }  // namespace lbrr
