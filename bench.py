@@ -19,8 +19,9 @@ roofline    dominant kernel (time-axis attention) timed live on its own stream
 cpu_baseline  the CPU oracle (PyTorch fp32 restatement; the reference has no
             CPU path) on a bounded sample, extrapolated to one chunk
 song        whole-song RTF (180.48 s, reference chunk plan)
-            at N GPUs: chunks dealt round-robin, per-chunk waveforms gathered to
-            rank 0 over NCCL and accumulated there in chunk order
+            at N GPUs through lbrr_separate_song: chunks dealt round-robin,
+            overlap strips exchanged between neighbouring chunks' GPUs, each GPU
+            copying its own finished samples to the host
 """
 from __future__ import annotations
 
@@ -214,6 +215,9 @@ def run_ours(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
+        # host-side barriers (the song phase): an NCCL barrier would leave a
+        # kernel waiting on each GPU that rank 0's song engines then run on
+        cpu_group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=300))
     pk = peaks()
     weights, audio = make_inputs(seed=rank)
     eng = lbrr.Engine(local_rank, CHUNK)
@@ -273,7 +277,7 @@ def run_ours(args, rank, world, local_rank):
         e2e_ms = float(t.item())
 
     # ---- whole song at N GPUs ----
-    song = run_song(torch, lbrr, eng, rank, world, dist)
+    song = run_song(torch, lbrr, eng, rank, world, dist, cpu_group if dist else None)
 
     result = None
     if rank == 0:
@@ -317,37 +321,53 @@ def run_ours(args, rank, world, local_rank):
     return result
 
 
-def run_song(torch, lbrr, eng, rank, world, dist):
+def run_song(torch, lbrr, eng, rank, world, dist, cpu_group=None):
     """180.48 s song, reference chunk plan (15 chunks), from host audio to host
-    stems.  1 GPU: lbrr_separate_song.  N GPUs: lbrr.song.separate_ranks (chunk
-    i on rank i % N, waveforms sent to rank 0 over NCCL, overlap-added there in
-    chunk order).  Wall time around the whole call, max over ranks."""
+    stems through lbrr_separate_song over `world` GPUs: rank 0 drives one engine
+    per local GPU (its own plus one on each other rank's device, weights loaded
+    in parallel threads) while the other ranks wait; chunk i runs on GPU i % N,
+    only the 1.4 MB overlap strip of each chunk boundary crosses devices
+    (NVLink), and every GPU copies its own finished samples to the host.  Wall
+    time around the call (the API is host-to-host and synchronous)."""
     from lbrr import song, synthetic
-    audio = synthetic.audio(SONG_LEN, seed=42)
     starts = song.chunk_starts(SONG_LEN)
-    info = {"audio_seconds": SONG_LEN / SR, "chunks": len(starts), "plan": "chunk 588800 / step 559360 / border 29440"}
-    if world == 1:
-        lbrr.separate([eng], audio)  # warm
+    info = {"audio_seconds": SONG_LEN / SR, "chunks": len(starts), "gpus": world,
+            "plan": "chunk 588800 / step 559360 / border 29440",
+            "exchange": "overlap strips between neighbouring chunks' GPUs (device-to-device); no NCCL"}
+    if dist:
         torch.cuda.synchronize()
+        dist.barrier(group=cpu_group)
+    result = None
+    if rank == 0:
+        audio = synthetic.audio(SONG_LEN, seed=42)
+        engines = [eng]
+        if world > 1:
+            import threading
+            weights = synthetic.checkpoint(seed=0)
+            extra = [None] * (world - 1)
+
+            def make(k):
+                e = lbrr.Engine(k + 1, CHUNK)
+                e.upload_weights(weights)
+                extra[k] = e
+            threads = [threading.Thread(target=make, args=(k,)) for k in range(world - 1)]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join()
+            if any(e is None for e in extra):
+                raise RuntimeError("could not create an engine on every GPU")
+            engines += extra
+        lbrr.separate(engines, audio)  # warm
         t0 = time.perf_counter()
-        lbrr.separate([eng], audio)
+        lbrr.separate(engines, audio)
         dt = time.perf_counter() - t0
-        return {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info}
-
-    def forward(x, y):
-        eng.bench_forward(x, y, stream=torch.cuda.current_stream())
-
-    dist.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    song.separate_ranks(forward, audio, rank, world, dist, "cuda")
-    torch.cuda.synchronize()
-    dt = time.perf_counter() - t0
-    t = torch.tensor([dt], device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dt = float(t.item())
-    return {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info,
-            "exchange": "per-chunk waveform [6][2][588800] fp32 sent to rank 0 over NCCL"}
+        for e in engines[1:]:
+            e.close()
+        result = {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info}
+    if dist:
+        dist.barrier(group=cpu_group)
+    return result
 
 
 # ---------------------------------------------------------------------------

@@ -144,9 +144,13 @@ void lbrr_engine_destroy(lbrr_engine* e);
 /* Whole song (replaces separate()'s GPU loop, src/main.rs:7617-7775): reflect
  * pad, chunk grid, per-chunk forward, fade-weighted overlap-add, division by
  * the fade energy, crop.  Chunks are dealt round-robin over the n_engines
- * engines (one per GPU, one host thread each); every chunk's ISTFT waveform
- * is copied peer-to-peer to engines[0]'s device and accumulated there in
- * chunk order, so the result does not depend on n_engines.
+ * engines (one per GPU, one host thread each, each engine listed once).  With
+ * the reference plan (chunks overlapping by less than half) every engine
+ * finishes the song samples its chunks start, receiving only the previous
+ * chunk's overlap strip from its neighbour engine (a device-to-device copy,
+ * over NVLink between GPUs), and copies them to host_out itself; the result
+ * is bit-identical to accumulating all chunks in order on one GPU, whatever
+ * n_engines is.  Plans overlapping by half or more accumulate on engines[0].
  * host_interleaved: [len][2]; host_out: [6][2][len]. */
 int lbrr_separate_song(lbrr_engine* const* engines, int n_engines, const float* host_interleaved, int64_t len,
                        const lbrr_chunk_plan* plan, float* host_out);

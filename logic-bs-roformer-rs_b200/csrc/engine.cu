@@ -5,11 +5,15 @@
 #include <cufft.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <condition_variable>
 #include <cmath>
 #include <cstring>
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/lbrr_gpu.h"
@@ -180,6 +184,17 @@ struct lbrr_engine {
   float* pin_out = nullptr;
   float* dev_in = nullptr;
   float* dev_out = nullptr;
+  // whole-song sharding (lbrr_separate_song): double-buffered pinned chunk
+  // input and region output, the finished region on the device, the overlap
+  // strip this engine produces, and the strips it receives (one per chunk)
+  float* song_pin_in[2] = {nullptr, nullptr};
+  float* song_pin_out[2] = {nullptr, nullptr};
+  float* song_fin = nullptr;
+  float* song_strip_out = nullptr;
+  float* song_strip_in = nullptr;
+  size_t song_strip_in_bytes = 0;
+  cudaEvent_t song_ev_in[2] = {nullptr, nullptr};
+  cudaEvent_t song_ev_out[2] = {nullptr, nullptr};
 };
 
 namespace {
@@ -402,6 +417,15 @@ extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
   cudaFree(e->sarena);
   if (e->pin_in) cudaFreeHost(e->pin_in);
   if (e->pin_out) cudaFreeHost(e->pin_out);
+  for (int i = 0; i < 2; ++i) {
+    if (e->song_pin_in[i]) cudaFreeHost(e->song_pin_in[i]);
+    if (e->song_pin_out[i]) cudaFreeHost(e->song_pin_out[i]);
+    if (e->song_ev_in[i]) cudaEventDestroy(e->song_ev_in[i]);
+    if (e->song_ev_out[i]) cudaEventDestroy(e->song_ev_out[i]);
+  }
+  cudaFree(e->song_fin);
+  cudaFree(e->song_strip_out);
+  cudaFree(e->song_strip_in);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -885,18 +909,10 @@ std::vector<int64_t> chunk_starts(int64_t len, int64_t chunk, int64_t step, int6
 }
 }  // namespace
 
-extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const float* xh, int64_t len,
-                                  const lbrr_chunk_plan* plan, float* outh) {
-  if (!engines || n <= 0 || !xh || !outh) return fail(LBRR_ERR_INVALID, "NULL argument");
-  if (len <= 0) return fail(LBRR_ERR_INVALID, "empty audio is unsupported");
-  const lbrr_chunk_plan P = plan ? *plan : lbrr_chunk_plan{588800, 559360, 29440};
-  if (P.chunk <= kNfft / 2 || P.step <= 0 || P.step > P.chunk || P.border < 0 || 2 * P.border > P.chunk)
-    return fail(LBRR_ERR_INVALID, "invalid chunk plan");
-  for (int i = 0; i < n; ++i) {
-    if (!engines[i]) return fail(LBRR_ERR_INVALID, "NULL engine");
-    if (!engines[i]->weights_loaded) return fail(LBRR_ERR_STATE, "weights not loaded");
-    if (engines[i]->max_len < P.chunk) return fail(LBRR_ERR_INVALID, "engine scratch smaller than the chunk");
-  }
+// Plans whose chunks overlap by more than half (a sample in three or more
+// chunks): every waveform is accumulated on engine 0 in chunk order.
+static int separate_song_serial(lbrr_engine* const* engines, int n, const float* xh, int64_t len,
+                                const lbrr_chunk_plan& P, float* outh) {
   const auto starts = chunk_starts(len, P.chunk, P.step, P.border);
   const int64_t needed = P.border + len;
   const int64_t right = starts.back() + P.chunk - needed;
@@ -1033,6 +1049,275 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
 
 // ---------------------------------------------------------------------------
 // Per-op entry points
+// ---------------------------------------------------------------------------
+// Whole song, sharded (every sample in at most two chunks: 2 * step >= chunk)
+// ---------------------------------------------------------------------------
+// Chunk c (padded offset s_c) belongs to engine c % n.  That engine produces
+// the song samples [s_c - border, s_{c+1} - border) (the first chunk from 0,
+// the last to the end): its head, where chunk c-1 also contributes, and the
+// part no other chunk covers.  The previous chunk's contribution to the head
+// arrives as an overlap strip y*w | w*w of (chunk - step) samples, copied
+// device to device (NVLink when the engines sit on different GPUs); nothing
+// else crosses devices.  Each sample is then
+//   (0 + y_{c-1} w_{c-1} + y_c w_c) / max(0 + w_{c-1}^2 + w_c^2, 1e-8)
+// with every product and sum rounded on its own, in chunk order: the same
+// fp32 operations, in the same order, as accumulating all chunks one after
+// the other (tools/bench_ref.py:47-65; IEEE addition is commutative, so the
+// two-term sums match exactly).  Each engine's host thread prepares its chunk
+// inputs (reflect padding at the song edges), drives its GPU, and copies its
+// finished regions into the caller's planar output.
+namespace {
+struct SongGeom {
+  int64_t C, step, border, ov, len;
+  int nc;
+  __host__ __device__ float fade(int64_t rel, int c) const {
+    // linear fade of width border; the first chunk keeps its leading edge, the last its trailing edge
+    if (rel < border && c != 0) return static_cast<float>(rel) / static_cast<float>(border);
+    if (rel >= C - border && c != nc - 1) return static_cast<float>(C - 1 - rel) / static_cast<float>(border);
+    return 1.0f;
+  }
+};
+
+// Overlap strip of chunk c: relative samples [step, C): 12 channels of y*w, then w*w.
+__global__ void song_strip_kernel(const float* __restrict__ y, float* __restrict__ strip, SongGeom g, int c) {
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j >= g.ov) return;
+  const int64_t rel = g.step + j;
+  const float w = g.fade(rel, c);
+  for (int ch = 0; ch < 2 * kStems; ++ch) strip[ch * g.ov + j] = __fmul_rn(y[ch * g.C + rel], w);
+  strip[2 * kStems * g.ov + j] = __fmul_rn(w, w);
+}
+
+// Finished song samples of chunk c: relative samples [r0, r0 + n), the first
+// `head` of them also carrying the previous chunk's strip.
+__global__ void song_region_kernel(const float* __restrict__ y, const float* __restrict__ strip_prev,
+                                   float* __restrict__ fin, SongGeom g, int c, int64_t r0, int64_t n, int64_t head) {
+  const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const int64_t rel = r0 + j;
+  const float w = g.fade(rel, c);
+  float den = __fmul_rn(w, w);
+  const bool both = rel < head;
+  if (both) den = __fadd_rn(strip_prev[2 * kStems * g.ov + rel], den);
+  den = fmaxf(den, 1e-8f);
+  for (int ch = 0; ch < 2 * kStems; ++ch) {
+    float num = __fmul_rn(y[ch * g.C + rel], w);
+    if (both) num = __fadd_rn(strip_prev[ch * g.ov + rel], num);
+    fin[ch * n + j] = __fdiv_rn(num, den);
+  }
+}
+
+struct SongRun {
+  std::atomic<int> abort{0};
+  std::mutex mu;
+  std::condition_variable cv;
+  std::vector<int> strip_ready;      // chunk c's strip is recorded in strip_ev[c]
+  std::vector<cudaEvent_t> strip_ev;  // created on the producing engine's device
+  std::vector<int> rc;
+  std::vector<std::string> msg;
+};
+
+int ensure_song_buffers(lbrr_engine* e, const SongGeom& g) {
+  const size_t in_b = static_cast<size_t>(g.C) * 2 * sizeof(float);
+  const size_t out_b = static_cast<size_t>(g.C) * 2 * kStems * sizeof(float);
+  const size_t strip_b = static_cast<size_t>(2 * kStems + 1) * g.ov * sizeof(float);
+  if (!e->song_fin) {
+    // sized for the largest chunk this engine takes
+    const size_t max_in = static_cast<size_t>(e->max_len) * 2 * sizeof(float);
+    const size_t max_out = static_cast<size_t>(e->max_len) * 2 * kStems * sizeof(float);
+    const size_t max_strip = static_cast<size_t>(2 * kStems + 1) * (e->max_len / 2 + 1) * sizeof(float);
+    for (int i = 0; i < 2; ++i) {
+      CK(cudaMallocHost(&e->song_pin_in[i], max_in));
+      CK(cudaMallocHost(&e->song_pin_out[i], max_out));
+      CK(cudaEventCreateWithFlags(&e->song_ev_in[i], cudaEventDisableTiming));
+      CK(cudaEventCreateWithFlags(&e->song_ev_out[i], cudaEventDisableTiming));
+    }
+    CK(cudaMalloc(&e->song_fin, max_out));
+    CK(cudaMalloc(&e->song_strip_out, max_strip));
+  }
+  (void)in_b;
+  (void)out_b;
+  const size_t need = strip_b * static_cast<size_t>(g.nc);
+  if (e->song_strip_in_bytes < need) {
+    cudaFree(e->song_strip_in);
+    e->song_strip_in = nullptr;
+    e->song_strip_in_bytes = 0;
+    CK(cudaMalloc(&e->song_strip_in, need));
+    e->song_strip_in_bytes = need;
+  }
+  return LBRR_OK;
+}
+
+void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, float* outh, const SongGeom g,
+                 const std::vector<int64_t>& starts, SongRun& run) {
+  lbrr_engine* e = engines[me];
+  DeviceGuard dg(e->device);
+  const size_t strip_b = static_cast<size_t>(2 * kStems + 1) * g.ov * sizeof(float);
+  auto bail = [&](int rc) {
+    run.rc[me] = rc;
+    run.msg[me] = lbrr_last_error();
+    run.abort.store(1);
+    run.cv.notify_all();
+  };
+  if (int rc = ensure_song_buffers(e, g)) return bail(rc);
+  // deferred host copy of the previous region (slot, song offset, length)
+  int pend_slot = -1;
+  int64_t pend_o0 = 0, pend_n = 0;
+  auto scatter = [&]() -> int {
+    if (pend_slot < 0) return LBRR_OK;
+    if (cudaEventSynchronize(e->song_ev_out[pend_slot]) != cudaSuccess) return fail(LBRR_ERR_CUDA, "region copy");
+    const float* src = e->song_pin_out[pend_slot];
+    for (int ch = 0; ch < 2 * kStems; ++ch)
+      std::memcpy(outh + static_cast<size_t>(ch) * g.len + pend_o0, src + static_cast<size_t>(ch) * pend_n,
+                  static_cast<size_t>(pend_n) * sizeof(float));
+    pend_slot = -1;
+    return LBRR_OK;
+  };
+  int k = 0;
+  for (int c = me; c < g.nc; c += n, ++k) {
+    if (run.abort.load()) return;
+    const int slot = k & 1;
+    const int64_t s = starts[c];
+    // chunk input: padded samples [s, s + C), reflected outside the song
+    if (cudaEventSynchronize(e->song_ev_in[slot]) != cudaSuccess) return bail(fail(LBRR_ERR_CUDA, "input slot"));
+    float* pin = e->song_pin_in[slot];
+    const int64_t lo = std::max<int64_t>(s, g.border), hi = std::min<int64_t>(s + g.C, g.border + g.len);
+    if (hi > lo) std::memcpy(pin + 2 * (lo - s), xh + 2 * (lo - g.border), static_cast<size_t>(hi - lo) * 2 * sizeof(float));
+    for (int64_t p = s; p < s + g.C; ++p) {
+      if (p >= lo && p < hi) {
+        p = hi - 1;
+        continue;
+      }
+      int64_t src = 0;
+      if (g.len > 1) {
+        const int64_t period = 2 * (g.len - 1);
+        int64_t q = (p - g.border) % period;
+        if (q < 0) q += period;
+        src = q < g.len ? q : period - q;
+      }
+      pin[2 * (p - s)] = xh[2 * src];
+      pin[2 * (p - s) + 1] = xh[2 * src + 1];
+    }
+    if (cudaMemcpyAsync(e->dev_in, pin, static_cast<size_t>(g.C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
+                        e->stream) != cudaSuccess ||
+        cudaEventRecord(e->song_ev_in[slot], e->stream) != cudaSuccess)
+      return bail(fail(LBRR_ERR_CUDA, "chunk upload"));
+    if (int rc = lbrr_forward_chunk(e, e->dev_in, g.C, e->dev_out, e->stream)) return bail(rc);
+    const unsigned blocks_ov = static_cast<unsigned>((g.ov + 255) / 256);
+    if (c + 1 < g.nc) {
+      // strip for the next chunk's engine
+      lbrr_engine* dst = engines[(c + 1) % n];
+      float* dst_strip = dst->song_strip_in + static_cast<size_t>(c) * (strip_b / sizeof(float));
+      song_strip_kernel<<<blocks_ov, 256, 0, e->stream>>>(e->dev_out, e->song_strip_out, g, c);
+      cudaError_t ce = cudaGetLastError();
+      if (ce == cudaSuccess)
+        ce = cudaMemcpyPeerAsync(dst_strip, dst->device, e->song_strip_out, e->device, strip_b, e->stream);
+      if (ce == cudaSuccess) ce = cudaEventRecord(run.strip_ev[c], e->stream);
+      if (ce != cudaSuccess) return bail(fail(LBRR_ERR_PEER, std::string("overlap strip: ") + cudaGetErrorString(ce)));
+      {
+        std::lock_guard<std::mutex> lk(run.mu);
+        run.strip_ready[c] = 1;
+      }
+      run.cv.notify_all();
+    }
+    // this chunk's finished samples
+    const int64_t o0 = c == 0 ? 0 : s - g.border;
+    const int64_t o1 = c + 1 < g.nc ? starts[c + 1] - g.border : g.len;
+    const int64_t r0 = o0 + g.border - s, nreg = o1 - o0, head = c > 0 ? g.ov : 0;
+    const float* strip_prev = nullptr;
+    if (c > 0) {
+      std::unique_lock<std::mutex> lk(run.mu);
+      // the previous chunk's engine records its strip; a failed engine raises abort
+      if (!run.cv.wait_for(lk, std::chrono::seconds(120), [&] { return run.strip_ready[c - 1] || run.abort.load(); }) ||
+          run.abort.load())
+        return run.abort.load() ? void() : bail(fail(LBRR_ERR_STATE, "overlap strip never arrived"));
+      lk.unlock();
+      if (cudaStreamWaitEvent(e->stream, run.strip_ev[c - 1], 0) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "strip wait"));
+      strip_prev = e->song_strip_in + static_cast<size_t>(c - 1) * (strip_b / sizeof(float));
+    }
+    if (nreg > 0) {
+      song_region_kernel<<<static_cast<unsigned>((nreg + 255) / 256), 256, 0, e->stream>>>(
+          e->dev_out, strip_prev, e->song_fin, g, c, r0, nreg, head);
+      if (cudaGetLastError() != cudaSuccess) return bail(fail(LBRR_ERR_CUDA, "region launch"));
+    }
+    // the host copy of the previous region overlaps this chunk's GPU work
+    if (int rc = scatter()) return bail(rc);
+    if (nreg > 0) {
+      if (cudaMemcpyAsync(e->song_pin_out[slot], e->song_fin, static_cast<size_t>(nreg) * 2 * kStems * sizeof(float),
+                          cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
+          cudaEventRecord(e->song_ev_out[slot], e->stream) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "region download"));
+      pend_slot = slot;
+      pend_o0 = o0;
+      pend_n = nreg;
+    }
+  }
+  if (int rc = scatter()) return bail(rc);
+  if (int rc = check_status(e->status, e->stream)) return bail(rc);
+}
+}  // namespace
+
+extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const float* xh, int64_t len,
+                                  const lbrr_chunk_plan* plan, float* outh) {
+  if (!engines || n <= 0 || !xh || !outh) return fail(LBRR_ERR_INVALID, "NULL argument");
+  if (len <= 0) return fail(LBRR_ERR_INVALID, "empty audio is unsupported");
+  const lbrr_chunk_plan P = plan ? *plan : lbrr_chunk_plan{588800, 559360, 29440};
+  if (P.chunk <= kNfft / 2 || P.step <= 0 || P.step > P.chunk || P.border < 0 || 2 * P.border > P.chunk)
+    return fail(LBRR_ERR_INVALID, "invalid chunk plan");
+  for (int i = 0; i < n; ++i) {
+    if (!engines[i]) return fail(LBRR_ERR_INVALID, "NULL engine");
+    if (!engines[i]->weights_loaded) return fail(LBRR_ERR_STATE, "weights not loaded");
+    if (engines[i]->max_len < P.chunk) return fail(LBRR_ERR_INVALID, "engine scratch smaller than the chunk");
+    for (int k = 0; k < i; ++k)
+      if (engines[k] == engines[i]) return fail(LBRR_ERR_INVALID, "the same engine is listed twice");
+  }
+  if (2 * P.step < P.chunk) return separate_song_serial(engines, n, xh, len, P, outh);
+  const auto starts = chunk_starts(len, P.chunk, P.step, P.border);
+  SongGeom g;
+  g.C = P.chunk;
+  g.step = P.step;
+  g.border = P.border;
+  g.ov = P.chunk - P.step;
+  g.len = len;
+  g.nc = static_cast<int>(starts.size());
+  const int workers = std::min<int>(n, g.nc);
+  SongRun run;
+  run.strip_ready.assign(g.nc, 0);
+  run.strip_ev.assign(g.nc, nullptr);
+  run.rc.assign(workers, LBRR_OK);
+  run.msg.assign(workers, std::string());
+  int rc = LBRR_OK;
+  for (int c = 0; rc == LBRR_OK && c + 1 < g.nc; ++c) {
+    DeviceGuard dg(engines[c % workers]->device);
+    if (cudaEventCreateWithFlags(&run.strip_ev[c], cudaEventDisableTiming) != cudaSuccess)
+      rc = fail(LBRR_ERR_CUDA, "event create");
+  }
+  if (rc == LBRR_OK) {
+    // every engine's receive buffers exist before any strip is sent
+    for (int i = 0; rc == LBRR_OK && i < workers; ++i) {
+      DeviceGuard dg(engines[i]->device);
+      rc = ensure_song_buffers(engines[i], g);
+    }
+  }
+  if (rc == LBRR_OK) {
+    std::vector<std::thread> th;
+    for (int i = 0; i < workers; ++i)
+      th.emplace_back(song_worker, engines, workers, i, xh, outh, g, std::cref(starts), std::ref(run));
+    for (auto& t : th) t.join();
+    for (int i = 0; i < workers && rc == LBRR_OK; ++i)
+      if (run.rc[i] != LBRR_OK) rc = fail(run.rc[i], run.msg[i]);
+    if (rc == LBRR_OK && run.abort.load()) rc = fail(LBRR_ERR_STATE, "song separation aborted");
+  }
+  for (int c = 0; c + 1 < g.nc; ++c)
+    if (run.strip_ev[c]) {
+      DeviceGuard dg(engines[c % workers]->device);
+      cudaEventSynchronize(run.strip_ev[c]);
+      cudaEventDestroy(run.strip_ev[c]);
+    }
+  return rc;
+}
+
 // ---------------------------------------------------------------------------
 static int* op_status() {
   static std::mutex mu;

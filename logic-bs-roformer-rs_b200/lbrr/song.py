@@ -64,14 +64,26 @@ def owned_chunks(n_chunks: int, rank: int, world: int) -> list:
     return list(range(rank, n_chunks, world))
 
 
+def _reflect_pad_dev(x, left: int, right: int):
+    """reflect_pad on a [2][L] torch tensor, as a gather on its own device."""
+    import torch
+    length = x.shape[-1]
+    if length == 1:
+        return x.expand(x.shape[0], left + 1 + right).contiguous()
+    idx = torch.arange(-left, length + right, device=x.device, dtype=torch.int64) % (2 * (length - 1))
+    idx = torch.where(idx < length, idx, 2 * (length - 1) - idx)
+    return x.index_select(1, idx)
+
+
 def separate_ranks(forward, audio_planar: np.ndarray, rank: int, world: int, dist=None, device="cpu",
                    chunk: int = CHUNK, step: int = STEP, border: int = BORDER):
     """Separate one song over ``world`` ranks.
 
     forward(x, out): x is a [chunk][2] fp32 tensor on ``device`` (interleaved
     stereo), out a [6][2][chunk] fp32 tensor it fills.  Every rank must call
-    this with the same audio and plan.  Returns the stems [6][2][length] as a
-    numpy array on rank 0 and None elsewhere.
+    this with the same audio and plan.  The song is copied to ``device`` once
+    (from pinned memory on a GPU) and padded and cut there.  Returns the stems
+    [6][2][length] as a numpy array on rank 0 and None elsewhere.
     """
     import torch
     if world > 1 and dist is None:
@@ -79,8 +91,15 @@ def separate_ranks(forward, audio_planar: np.ndarray, rank: int, world: int, dis
     length = audio_planar.shape[-1]
     starts = chunk_starts(length, chunk, step, border)
     needed = border + length
-    xp = reflect_pad(np.asarray(audio_planar, dtype=np.float32), border, starts[-1] + chunk - needed)
+    dev = torch.device(device)
+    on_gpu = dev.type == "cuda"
+    x = torch.from_numpy(np.ascontiguousarray(audio_planar, dtype=np.float32))
+    x = x.pin_memory().to(dev, non_blocking=True) if on_gpu else x
+    xp = _reflect_pad_dev(x, border, starts[-1] + chunk - needed)
     mine = owned_chunks(len(starts), rank, world)
+
+    def chunk_input(s):
+        return xp[:, s:s + chunk].t().contiguous()
 
     # Non-zero ranks: forward every owned chunk, send each waveform to rank 0 in
     # chunk order (point-to-point pairs match because both sides walk the same
@@ -89,33 +108,40 @@ def separate_ranks(forward, audio_planar: np.ndarray, rank: int, world: int, dis
     if rank != 0:
         outs = []
         for i in mine:
-            x = torch.from_numpy(np.ascontiguousarray(xp[:, starts[i]:starts[i] + chunk].T)).to(device)
-            y = torch.empty(6, 2, chunk, dtype=torch.float32, device=device)
-            forward(x, y)
+            y = torch.empty(6, 2, chunk, dtype=torch.float32, device=dev)
+            forward(chunk_input(starts[i]), y)
             outs.append(y)
             dist.send(y, dst=0)
-        if torch.device(device).type == "cuda":
+        if on_gpu:
             torch.cuda.current_stream().synchronize()  # the sends read `outs` until here
         return None
 
-    result = torch.zeros(12, needed, dtype=torch.float32, device=device)
-    counter = torch.zeros(needed, dtype=torch.float32, device=device)
-    own = torch.empty(6, 2, chunk, dtype=torch.float32, device=device)
-    recv = torch.empty(6, 2, chunk, dtype=torch.float32, device=device)
+    result = torch.zeros(12, needed, dtype=torch.float32, device=dev)
+    counter = torch.zeros(needed, dtype=torch.float32, device=dev)
+    own = torch.empty(6, 2, chunk, dtype=torch.float32, device=dev)
+    recv = torch.empty(6, 2, chunk, dtype=torch.float32, device=dev)
+    fades = {}
     for i, s in enumerate(starts):
         owner = i % world
         if owner == 0:
-            x = torch.from_numpy(np.ascontiguousarray(xp[:, s:s + chunk].T)).to(device)
-            forward(x, own)
+            forward(chunk_input(s), own)
             y = own
         else:
             dist.recv(recv, src=owner)
             y = recv
-        w = torch.from_numpy(chunk_weights(i, len(starts), chunk, border)).to(device)
+        key = (i == 0, i == len(starts) - 1)  # the fade depends only on these
+        if key not in fades:
+            fades[key] = torch.from_numpy(chunk_weights(i, len(starts), chunk, border)).to(dev)
+        w = fades[key]
         take = min(chunk, needed - s)
         result[:, s:s + take] += y.reshape(12, chunk)[:, :take] * w[:take]
         counter[s:s + take] += w[:take] * w[:take]
     if not bool((counter[border:needed] > 0).all()):
         raise RuntimeError("uncovered audio tail")
-    out = (result / counter.clamp_min(1e-8))[:, border:needed]
-    return out.reshape(6, 2, length).cpu().numpy()
+    out = (result / counter.clamp_min(1e-8))[:, border:needed].reshape(6, 2, length)
+    if not on_gpu:
+        return out.numpy()
+    host = torch.empty(out.shape, dtype=torch.float32, pin_memory=True)
+    host.copy_(out, non_blocking=True)
+    torch.cuda.current_stream().synchronize()
+    return host.numpy()

@@ -118,4 +118,5 @@ def test_song_demix_matches_oracle_plan(engine):
         return engine.forward_host(interleave(chunk_planar))
 
     ref = R.demix(model, audio)
-    assert snr_db(got, ref) > 100.0
+    # same fp32 products, sums and divisions in the same chunk order: bit-equal
+    assert np.array_equal(got, ref), snr_db(got, ref)

@@ -1,12 +1,14 @@
 """Whole-song separation on B200s: the rank-sharded driver (lbrr.song) over the
 engine's device-buffer forward gives the oracle's chunked demix of the same
-per-chunk model bit for bit, and the multi-engine C entry point
-(lbrr_separate_song over two GPUs, chunks dealt round-robin, stitched on the
-first) gives exactly the one-GPU result."""
+per-chunk model bit for bit, and so does the multi-engine C entry point
+(lbrr_separate_song: chunks dealt round-robin, each engine finishing its own
+samples from its chunks and the previous chunk's overlap strip), for one
+engine, two engines on one GPU and two GPUs alike."""
 import numpy as np
 import pytest
 import torch
 
+from helpers import snr_db
 from oracle import bsroformer_ref as R
 
 pytestmark = pytest.mark.gpu
@@ -41,6 +43,40 @@ def test_separate_ranks_one_process_matches_demix(weights):
         assert np.array_equal(got, ref)
     finally:
         eng.close()
+
+
+def test_two_engines_one_gpu_match_oracle(weights):
+    # the overlap strips travel between engines even on one device
+    import lbrr
+    e0, e1 = _engine(0, weights), _engine(0, weights)
+    try:
+        audio = R.synth_audio(2 * R.CHUNK + 12345, seed=17)  # 3 chunks
+        two = lbrr.separate([e0, e1], audio)
+        one = lbrr.separate([e0], audio)
+        ref = R.demix(lambda c: e0.forward_host(np.ascontiguousarray(c.T)), audio)
+        assert np.array_equal(two, one)
+        assert np.array_equal(one, ref)
+    finally:
+        e1.close()
+        e0.close()
+
+
+def test_short_song_and_serial_plan(weights):
+    # one chunk (shorter than the plan's chunk), and a plan whose chunks overlap
+    # by more than half (accumulated on one engine in chunk order)
+    import lbrr
+    e0 = _engine(0, weights)
+    try:
+        audio = R.synth_audio(50000, seed=19)
+        got = lbrr.separate([e0], audio, chunk=65536, step=60000, border=5536)
+        ref = R.demix(lambda c: e0.forward_host(np.ascontiguousarray(c.T)), audio, 65536, 60000, 5536)
+        assert np.array_equal(got, ref)
+        audio = R.synth_audio(200000, seed=23)
+        got = lbrr.separate([e0], audio, chunk=65536, step=20000, border=8192)
+        ref = R.demix(lambda c: e0.forward_host(np.ascontiguousarray(c.T)), audio, 65536, 20000, 8192)
+        assert snr_db(got, ref) > 100.0
+    finally:
+        e0.close()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
