@@ -302,7 +302,7 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": round(e2e_ms / world, 4), "unit": UNIT, "h2d_bytes_per_step": CHUNK * 2 * 4 * world,
                     "d2h_bytes_per_step": 6 * 2 * CHUNK * 4 * world},
             "gpu_launches": LAUNCHES_PER_CHUNK * args.steps * world,
-            "roofline": {"kernel": "attention time axis (attn_kernel, T=1151, 496 sequences)", "bound": "tensor",
+            "roofline": {"kernel": "attention time axis (attn_time_kernel, T=1151, 496 sequences)", "bound": "tensor",
                          "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["tflops"], 4), "traffic": traffic,
                          "peak_source": pk["source"] + " dense bf16 burst (MEASURED_PEAKS.json)"},
