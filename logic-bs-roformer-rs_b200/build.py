@@ -23,6 +23,10 @@ CSRC = HERE / "csrc"
 INCLUDE = HERE.parent / "include"
 BUILD = HERE / "_build"
 LIB = HERE / "lbrr" / "liblbrr_b200.so"
+HOST = HERE / "host"
+CLI = HERE / "lbrr" / "lbrr_b200"
+CXX = os.environ.get("CXX", "g++")
+CUDA_HOME = Path(NVCC_DIR := os.path.dirname(os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc"))).parent
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-O2", "--expt-relaxed-constexpr",
@@ -63,7 +67,27 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
+    build_cli(verbose)
     return LIB
+
+
+def build_cli(verbose: bool = False) -> Path:
+    """The host command-line front end (host/*.cpp), linked against the engine
+    library it sits next to (rpath $ORIGIN) and the CUDA runtime."""
+    srcs = sorted(HOST.glob("*.cpp"))
+    deps = srcs + sorted(HOST.glob("*.h")) + [LIB, INCLUDE / "lbrr_gpu.h"]
+    if CLI.exists() and CLI.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
+        return CLI
+    cmd = [CXX, "-O2", "-std=c++17", "-Wall", "-I", str(CUDA_HOME / "include"), *map(str, srcs), "-o", str(CLI),
+           "-L", str(LIB.parent), "-llbrr_b200", "-L", str(CUDA_HOME / "lib64"), "-lcudart", "-lpthread",
+           "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise RuntimeError("host CLI build failed")
+    return CLI
 
 
 if __name__ == "__main__":
