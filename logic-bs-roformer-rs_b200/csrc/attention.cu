@@ -3,19 +3,17 @@
 // Replaces cuDNN SDPA + sdpa_gate of the reference (src/main.rs:6181-6199) and
 // its hand-written fallbacks attn_flash_tc / attn_flash_async (:3796-4312).
 // Q and K arrive already rotated (the QKV GEMM epilogue applies RoPE), V raw,
-// all inside the folded qkv tensor [M][1536] fp16 (token = t*nb + b).
-//
-// One CTA owns 128 query rows of one (sequence, head):
-//   time axis  sequence = band b, keys = all T frames (TMA 3-D box gathers the
-//              rows t*nb + b), key tiles of 128, online softmax;
-//   freq axis  two sequences (frames 2p, 2p+1) of nb = 62 bands packed into
-//              one 128-row tile (block-diagonal mask), a single key tile.
-// Pipeline (192 threads): warp 0 TMA (Q once, K/V double-buffered), warp 1
-// issues S = Q K^T (TMEM cols 0..127) and O += P V (TMEM cols 128..191; P read
-// from TMEM cols 192..255, V an MN-major shared-memory operand), warps 2..5 run
-// the softmax with one query row per thread, write P (fp16 pairs) to TMEM,
-// rescale O in TMEM, and finally write f16(f16(O/l) * sigmoid(gate)).  Keeping
-// P in TMEM halves the shared-memory traffic of a key tile.
+// all inside the folded qkv tensor [M][1536] fp16 (token = t*nb + b).  Both
+// kernels compute S = Q K^T into TMEM, run the softmax with one query row per
+// thread, write P (fp16 pairs) back to TMEM, form O += P V with P read from
+// TMEM (TS-form MMA, V an MN-major shared-memory operand) and finish with
+// f16(f16(O / l) * sigmoid(gate)):
+//   attn_time_kernel  time axis, sequence = one band's T frames (a 3-D TMA box
+//                     gathers rows t*nb + b), two 128-row query tiles per CTA,
+//                     128-key tiles with an online softmax;
+//   attn_freq_kernel  frequency axis, frames 2p and 2p+1 (62 bands each)
+//                     packed into one 128-row tile with a block-diagonal mask,
+//                     persistent CTAs walking (frame pair, head) items.
 #include "common.cuh"
 #include "exp2_poly.cuh"
 #include "kernels.h"
@@ -24,12 +22,6 @@ namespace lbrr {
 
 namespace {
 constexpr int kTile = 16384;  // one [128][64] fp16 tile
-constexpr int kOffQ = 0;
-constexpr int kOffK = kTile;
-constexpr int kOffV = 3 * kTile;
-constexpr int kOffBar = 5 * kTile;
-constexpr int kAttnSmem = kOffBar + 128;
-constexpr int kAttnThreads = 192;
 constexpr uint32_t kAttnTmemCols = 256;
 constexpr uint32_t kColS = 0;
 constexpr uint32_t kColO = 128;
@@ -48,276 +40,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__global__ void __launch_bounds__(kAttnThreads, 2)
-    attn_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
-  extern __shared__ __align__(1024) uint8_t smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;
-  uint64_t* p_full = bars + 6;
-  uint64_t* pv_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-  if ((smem_u32(smem) & 1023u) != 0) {
-    if (threadIdx.x == 0) report_status(a.status, kDevSmemMisaligned);
-    return;
-  }
-  const int nb = a.nb, T = a.T, nk = a.nk;
-  const bool time_axis = a.axis == 0;
-  const int head = time_axis ? (blockIdx.y & 7) : blockIdx.y;
-  const int band = time_axis ? (blockIdx.y >> 3) : 0;
-  const int qt = blockIdx.x;  // query tile (time) or sequence pair (freq)
-  const int row0 = qt * 2 * nb;  // freq axis: first token of the pair
-
-  if (threadIdx.x == 0) {
-    mbar_init(q_full, 1);
-    mbar_init(&kv_full[0], 1);
-    mbar_init(&kv_full[1], 1);
-    mbar_init(&kv_empty[0], 1);
-    mbar_init(&kv_empty[1], 1);
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
-    *abort_flag = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) tma_prefetch(&tm);
-  if (warp == 1) {
-    tmem_alloc(tmem_slot, kAttnTmemCols);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-
-  if (warp == 0) {
-    // ---------------- TMA producer ----------------
-    if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kTile);
-      if (time_axis)
-        tma_load_3d(smem + kOffQ, &tm, q_full, head * 64, band, qt * 128);
-      else
-        tma_load_2d(smem + kOffQ, &tm, q_full, head * 64, row0);
-      for (int j = 0; j < nk; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1u, abort_flag, a.status)) break;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * kTile);
-        if (time_axis) {
-          tma_load_3d(smem + kOffK + s * kTile, &tm, &kv_full[s], 512 + head * 64, band, j * 128);
-          tma_load_3d(smem + kOffV + s * kTile, &tm, &kv_full[s], 1024 + head * 64, band, j * 128);
-        } else {
-          tma_load_2d(smem + kOffK + s * kTile, &tm, &kv_full[s], 512 + head * 64, row0);
-          tma_load_2d(smem + kOffV + s * kTile, &tm, &kv_full[s], 1024 + head * 64, row0);
-        }
-      }
-    }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t id_s = idesc_f16_f32(128, 128);
-      const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
-      const uint32_t sq = smem_u32(smem + kOffQ);
-      auto issue_s = [&](int s) {
-        const uint32_t sk = smem_u32(smem + kOffK + s * kTile);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tmem + kColS, sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
-                     k > 0 ? 1u : 0u);
-      };
-      auto issue_pv = [&](int s, bool acc) {
-        const uint32_t sv = smem_u32(smem + kOffV + s * kTile);
-        // A = P from TMEM: 16 keys per MMA = 8 packed columns
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
-                     (acc || kk > 0) ? 1u : 0u);
-      };
-      bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
-      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag, a.status);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-        mma_commit(s_full);
-      }
-      for (int j = 0; ok && j < nk; ++j) {
-        ok = mbar_wait(p_full, j & 1, abort_flag, a.status);
-        if (!ok) break;
-        tc_fence_after();
-        if (j + 1 < nk) {
-          const int s1 = (j + 1) & 1;
-          ok = mbar_wait(&kv_full[s1], ((j + 1) >> 1) & 1, abort_flag, a.status);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(s1);
-          mma_commit(s_full);
-        }
-        issue_pv(j & 1, j > 0);
-        mma_commit(pv_done);
-        mma_commit(&kv_empty[j & 1]);
-      }
-    }
-  } else {
-    // ---------------- softmax + epilogue (one query row per thread) ----------------
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const uint32_t tS = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColS;
-    const uint32_t tO = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColO;
-    const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
-    const int rseq = r / nb;                        // freq axis: which packed sequence
-    const uint32_t tP = tmem + (static_cast<uint32_t>(q * 32) << 16) + kColP;
-    float m_run = -INFINITY, l_run = 0.f;
-    bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      ok = mbar_wait(s_full, j & 1, abort_flag, a.status);
-      if (!ok) break;
-      tc_fence_after();
-      const int key0 = j * 128;
-      // valid keys of this row inside the tile: [lo, hi)
-      const int lo = time_axis ? 0 : rseq * nb;
-      const int hi = time_axis ? min(128, T - key0) : lo + nb;
-      const bool full = lo == 0 && hi >= 128;  // warp-uniform on the time axis
-      // the whole S row (128 fp32) in registers: four loads, one wait
-      uint32_t s[4][32];
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(tS + q4 * 32, s[q4]);
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld_wait(s[q4]);
-      float mx = -INFINITY;
-      if (full) {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-          for (int k = 0; k < 32; ++k) mx = fmaxf(mx, __uint_as_float(s[q4][k]));
-      } else {
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-          for (int k = 0; k < 32; ++k)
-            if (q4 * 32 + k >= lo && q4 * 32 + k < hi) mx = fmaxf(mx, __uint_as_float(s[q4][k]));
-      }
-      const float m_new = fmaxf(m_run, mx);
-      // Keep the running reference max unless the row max grew by more than
-      // 2^8 in exp2 units: exponents stay <= 2^8 (exact enough in fp32 and in
-      // the fp16 P), and O needs no rescale on most tiles.
-      float m_use, corr, m_next;
-      if (m_run == -INFINITY || (m_new - m_run) * sc > 8.0f) {
-        m_use = m_new == -INFINITY ? 0.f : m_new;
-        corr = ex2((m_run - m_use) * sc);
-        m_next = m_new;
-      } else {
-        m_use = m_run;
-        corr = 1.0f;
-        m_next = m_run;
-      }
-      const float msc = m_use * sc;
-      // p = 2^(s*sc - m*sc) into fp16 pairs: packed fp32x2 FMA for the exponent
-      // argument and packed adds for the row sum, one MUFU ex2 per element.
-      // Computed before waiting for PV_{j-1}, so it overlaps that MMA.
-      uint32_t w[64];
-      float2 sum2 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const int c0 = q4 * 32 + 2 * k;
-          const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(s[q4][2 * k]), __uint_as_float(s[q4][2 * k + 1])),
-                                       make_float2(sc, sc), make_float2(-msc, -msc));
-          float2 p = make_float2(ex2(a2.x), ex2(a2.y));
-          if (!full) {
-            p.x = (c0 >= lo && c0 < hi) ? p.x : 0.f;
-            p.y = (c0 + 1 >= lo && c0 + 1 < hi) ? p.y : 0.f;
-          }
-          sum2 = __fadd2_rn(sum2, p);
-          w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
-        }
-      }
-      const float sum = sum2.x + sum2.y;
-      if (j > 0) {
-        // PV_{j-1} must be done before O is rescaled and P is overwritten
-        ok = mbar_wait(pv_done, (j - 1) & 1, abort_flag, a.status);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, corr != 1.0f)) {
-#pragma unroll 1
-          for (int c = 0; c < 64; c += 32) {
-            uint32_t v[32];
-            tmem_ld32(tO + c, v);
-            tmem_ld_wait(v);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              const float2 o = __fmul2_rn(make_float2(__uint_as_float(v[2 * k]), __uint_as_float(v[2 * k + 1])),
-                                          make_float2(corr, corr));
-              v[2 * k] = __float_as_uint(o.x);
-              v[2 * k + 1] = __float_as_uint(o.y);
-            }
-            tmem_st32(tO + c, v);
-          }
-          tmem_st_wait();
-        }
-      }
-      // P row r into TMEM lane r: column c holds keys (2c, 2c+1)
-      {
-        uint32_t* w0 = w;
-        uint32_t* w1 = w + 32;
-        tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(w0));
-        tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(w1));
-        tmem_st_wait();
-      }
-      l_run = l_run * corr + sum;
-      m_run = m_next;
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    if (ok) ok = mbar_wait(pv_done, (nk - 1) & 1, abort_flag, a.status);
-    tc_fence_after();
-    if (ok && !*abort_flag) {
-      bool valid;
-      int token;
-      if (time_axis) {
-        const int qi = qt * 128 + r;
-        valid = qi < T;
-        token = qi * nb + band;
-      } else {
-        const int t = qt * 2 + rseq;
-        valid = r < 2 * nb && t < T;
-        token = t * nb + (r - rseq * nb);
-      }
-      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      float sig = 0.f;
-      if (valid) sig = 1.0f / (1.0f + __expf(-__ldg(a.gates + static_cast<size_t>(token) * 8 + head)));
-#pragma unroll 1
-      for (int c = 0; c < 64; c += 32) {
-        uint32_t v[32];
-        tmem_ld32(tO + c, v);
-        tmem_ld_wait(v);
-        if (!valid) continue;
-        uint32_t w[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) {
-          const float o0 = f16_round(__uint_as_float(v[2 * k]) * inv);
-          const float o1 = f16_round(__uint_as_float(v[2 * k + 1]) * inv);
-          w[k] = pack_f16x2(o0 * sig, o1 * sig);
-        }
-        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(token) * 512 + head * 64 + c);
-        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        dst[2] = make_uint4(w[8], w[9], w[10], w[11]);
-        dst[3] = make_uint4(w[12], w[13], w[14], w[15]);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc(tmem, kAttnTmemCols);
-  }
-}
 // ---------------------------------------------------------------------------
 // Time axis: two query tiles per CTA, ping-pong between tensor core and softmax
 // ---------------------------------------------------------------------------
@@ -623,13 +345,219 @@ __global__ void __launch_bounds__(kT2Threads, 1)
     tmem_dealloc(tmem, kT2TmemCols);
   }
 }
+// ---------------------------------------------------------------------------
+// Frequency axis: persistent CTAs, one (frame pair, head) item at a time
+// ---------------------------------------------------------------------------
+// Each item is two sequences of nb = 62 band tokens (frames 2p and 2p+1) packed
+// into one 128-row tile with a block-diagonal mask, one key tile.  An item is
+// small (48 KB of Q/K/V), so its load latency, not its math, set the time of a
+// one-item CTA; here each CTA (two per SM) walks items with a stride of the
+// grid and a 2-stage TMA ring: item k+1's Q/K/V arrive while item k runs.
+// TMEM (256 columns): S 0..127, O 128..191, P 192..255.  Warp 0 loads, warp 1
+// issues S = Q K^T once the previous item's output has left TMEM and O = P V
+// once P is written, warps 2..5 run the softmax (one row per thread, only the
+// row's own sequence as keys) and the epilogue f16(f16(O/l) * sigmoid(gate)).
+constexpr int kFStages = 2;
+constexpr int kFStage = 3 * kTile;  // Q, K, V
+constexpr int kFOffBar = kFStages * kFStage;
+constexpr int kFSmem = kFOffBar + 128;
+constexpr int kFThreads = 192;
+
+__global__ void __launch_bounds__(kFThreads, 2)
+    attn_freq_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a, int n_items) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFOffBar);
+  uint64_t* full = bars + 0;       // [2]
+  uint64_t* empty = bars + 2;      // [2]
+  uint64_t* s_full = bars + 4;
+  uint64_t* p_full = bars + 5;
+  uint64_t* o_full = bars + 6;
+  uint64_t* tmem_free = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) report_status(a.status, kDevSmemMisaligned);
+    return;
+  }
+  const int nb = a.nb, T = a.T;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kFStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(o_full, 1);
+    mbar_init(tmem_free, 128);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) tma_prefetch(&tm);
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kAttnTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int k = 0;
+      for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++k) {
+        const int st = k & 1;
+        if (!mbar_wait(&empty[st], ((k >> 1) & 1) ^ 1u, abort_flag, a.status)) break;
+        const int head = it & 7, row0 = (it >> 3) * 2 * nb;
+        uint8_t* s = smem + st * kFStage;
+        mbar_arrive_expect_tx(&full[st], 3 * kTile);
+        tma_load_2d(s, &tm, &full[st], head * 64, row0);
+        tma_load_2d(s + kTile, &tm, &full[st], 512 + head * 64, row0);
+        tma_load_2d(s + 2 * kTile, &tm, &full[st], 1024 + head * 64, row0);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t id_s = idesc_f16_f32(128, 128);
+      const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
+      bool ok = true;
+      int k = 0;
+      for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++k) {
+        const int st = k & 1;
+        const uint32_t sq = smem_u32(smem + st * kFStage), sk = sq + kTile, sv = sq + 2 * kTile;
+        ok = mbar_wait(&full[st], (k >> 1) & 1, abort_flag, a.status);
+        // the previous item's softmax and epilogue are done with S, P and O
+        if (ok && k > 0) ok = mbar_wait(tmem_free, (k - 1) & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + kColS, sdesc_sw128(sq + kk * 32, 1024, 16), sdesc_sw128(sk + kk * 32, 1024, 16), id_s,
+                     kk > 0 ? 1u : 0u);
+        mma_commit(s_full);
+        ok = mbar_wait(p_full, k & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
+                     kk > 0 ? 1u : 0u);
+        mma_commit(o_full);
+        mma_commit(&empty[st]);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue (one row per thread) ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    const uint32_t tS = tmem + lane_off + kColS, tO = tmem + lane_off + kColO, tP = tmem + lane_off + kColP;
+    const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
+    const int rseq = r / nb;                        // which of the two packed sequences
+    const int lo = rseq * nb, hi = lo + nb;         // this row's keys
+    bool ok = true;
+    int k = 0;
+    for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++k) {
+      const int head = it & 7, t = (it >> 3) * 2 + rseq;
+      const bool valid = r < 2 * nb && t < T;
+      const int token = t * nb + (r - lo);
+      // the gate is independent of the MMAs: fetch it before waiting
+      const float gate = valid ? __ldg(a.gates + static_cast<size_t>(token) * 8 + head) : 0.f;
+      ok = mbar_wait(s_full, k & 1, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      // Two passes over S in 32-key chunks (S stays in TMEM until the next
+      // item): the row max, then the exponentials, each chunk's P stored as it
+      // is done.  A chunk none of the warp's rows has keys in is skipped; its
+      // P is written as zeros, since the PV MMA reads all 128 keys.
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        if (!__any_sync(0xffffffffu, q4 * 32 < hi && q4 * 32 + 32 > lo)) continue;
+        uint32_t v[32];
+        tmem_ld32(tS + q4 * 32, v);
+        tmem_ld_wait(v);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (q4 * 32 + c >= lo && q4 * 32 + c < hi) mx = fmaxf(mx, __uint_as_float(v[c]));
+      }
+      const float msc = (mx == -INFINITY ? 0.f : mx) * sc;
+      float2 sum2 = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t w[16];
+        if (__any_sync(0xffffffffu, q4 * 32 < hi && q4 * 32 + 32 > lo)) {
+          uint32_t v[32];
+          tmem_ld32(tS + q4 * 32, v);
+          tmem_ld_wait(v);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int c0 = q4 * 32 + 2 * c;
+            const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1])),
+                                         make_float2(sc, sc), make_float2(-msc, -msc));
+            float2 p = make_float2(ex2(a2.x), ex2(a2.y));
+            p.x = (c0 >= lo && c0 < hi) ? p.x : 0.f;
+            p.y = (c0 + 1 >= lo && c0 + 1 < hi) ? p.y : 0.f;
+            sum2 = __fadd2_rn(sum2, p);
+            w[c] = pack_f16x2(p.x, p.y);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) w[c] = 0u;
+        }
+        tmem_st16(tP + q4 * 16, w);
+      }
+      const float l = sum2.x + sum2.y;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      ok = mbar_wait(o_full, k & 1, abort_flag, a.status);
+      if (!ok) break;
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.0f / l : 0.f;
+      const float sig = valid ? 1.0f / (1.0f + __expf(-gate)) : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t v[32];
+        tmem_ld32(tO + c, v);
+        tmem_ld_wait(v);
+        if (!valid) continue;
+        uint32_t o16[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const float o0 = f16_round(__uint_as_float(v[2 * j]) * inv);
+          const float o1 = f16_round(__uint_as_float(v[2 * j + 1]) * inv);
+          o16[j] = pack_f16x2(o0 * sig, o1 * sig);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(token) * 512 + head * 64 + c);
+        dst[0] = make_uint4(o16[0], o16[1], o16[2], o16[3]);
+        dst[1] = make_uint4(o16[4], o16[5], o16[6], o16[7]);
+        dst[2] = make_uint4(o16[8], o16[9], o16[10], o16[11]);
+        dst[3] = make_uint4(o16[12], o16[13], o16[14], o16[15]);
+      }
+      // S, P and O may now be overwritten by the next item
+      tc_fence_before();
+      mbar_arrive(tmem_free);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kAttnTmemCols);
+  }
+}
 }  // namespace
 
 cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
                           cudaStream_t st) {
   static unsigned long long configured = 0;
   cudaError_t ce = once_per_device(configured, [] {
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    cudaError_t e = cudaFuncSetAttribute(attn_freq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
     if (e == cudaSuccess)
       e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
     if (e != cudaSuccess) return e;
@@ -653,7 +581,6 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   a.nb = nb;
   a.axis = axis;
   a.status = status;
-  dim3 grid;
   if (axis == 0) {
     e = make_map_3d(&tm, qkv, 1536, nb, T, 1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
     if (e != cudaSuccess) return e;
@@ -661,13 +588,17 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     // two query tiles per CTA
     attn_time_kernel<<<dim3((a.nk + 1) / 2, nb * 8), kT2Threads, kT2Smem, st>>>(tm, a);
     return cudaGetLastError();
-  } else {
-    e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
-    a.nk = 1;
-    grid = dim3((T + 1) / 2, 8);
   }
+  e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
   if (e != cudaSuccess) return e;
-  attn_kernel<<<grid, kAttnThreads, kAttnSmem, st>>>(tm, a);
+  a.nk = 1;
+  // (frame pair, head) items over two persistent CTAs per SM
+  const int n_items = (T + 1) / 2 * 8;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = n_items < 2 * sms ? n_items : 2 * sms;
+  attn_freq_kernel<<<grid, kFThreads, kFSmem, st>>>(tm, a, n_items);
   return cudaGetLastError();
 }
 
