@@ -114,8 +114,10 @@ int lbrr_check_safetensors(const char* path);
 int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);
 
 /* End to end from host memory: stage x_host through pinned memory, copy to
- * the device, forward, copy the stems back, synchronise, check the device
- * status.  x_host: [len][2], stems_host: [6][2][len]. */
+ * the device, forward, copy the stems back in slices (host threads move each
+ * slice into stems_host as it arrives), synchronise, check the device status.
+ * Replaces bench_forward plus the D2H of src/main.rs:7303-7317.
+ * x_host: [len][2], stems_host: [6][2][len]. */
 int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, float* stems_host);
 
 /* Front end and the first n_steps transformer axes only (n_steps in 0..24;

@@ -145,6 +145,8 @@ struct StepWeights {
   float *norm_g, *gate_w, *gate_b, *ff_g, *b1, *b2;
 };
 
+constexpr int kHostSlices = 8;  // slices of the stem download in lbrr_forward_chunk_host
+
 struct lbrr_engine {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -203,6 +205,8 @@ struct lbrr_engine {
   int64_t graph_len = -1;
   cudaStream_t graph_stream = nullptr;
   int graph_seen = 0;
+  // lbrr_forward_chunk_host: one event per downloaded slice of the stems
+  cudaEvent_t host_ev[kHostSlices] = {};
 };
 
 namespace {
@@ -435,6 +439,8 @@ extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
   cudaFree(e->song_strip_out);
   cudaFree(e->song_strip_in);
   if (e->graph) cudaGraphExecDestroy(e->graph);
+  for (auto& ev : e->host_ev)
+    if (ev) cudaEventDestroy(ev);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -923,17 +929,65 @@ extern "C" int lbrr_engine_sync(lbrr_engine* e) {
   return check_status(e->status, e->stream);
 }
 
+// Host memcpy split over `n` threads (one stream of bytes per thread).
+static void parallel_memcpy(void* dst, const void* src, size_t bytes, int n) {
+  if (n <= 1 || bytes < (1u << 20)) {
+    std::memcpy(dst, src, bytes);
+    return;
+  }
+  std::vector<std::thread> th;
+  const size_t part = (bytes / n + 63) / 64 * 64;
+  for (int i = 1; i < n; ++i) {
+    const size_t o = part * i;
+    if (o >= bytes) break;
+    th.emplace_back([=] {
+      std::memcpy(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, std::min(part, bytes - o));
+    });
+  }
+  std::memcpy(dst, src, std::min(part, bytes));
+  for (auto& t : th) t.join();
+}
+
+// The stems leave the GPU in kHostSlices slices, each followed by an event;
+// host threads copy a slice from pinned memory into the caller's buffer as
+// soon as it has arrived, so the host copy overlaps the rest of the download.
 extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t len, float* outh) {
   if (int rc = check_forward_args(e, xh, len, outh)) return rc;
   DeviceGuard g(e->device);
   const size_t in_b = static_cast<size_t>(len) * 2 * sizeof(float);
   const size_t out_b = static_cast<size_t>(len) * 2 * kStems * sizeof(float);
-  std::memcpy(e->pin_in, xh, in_b);
+  for (auto& ev : e->host_ev)
+    if (!ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  parallel_memcpy(e->pin_in, xh, in_b, 4);
   CK(cudaMemcpyAsync(e->dev_in, e->pin_in, in_b, cudaMemcpyHostToDevice, e->stream));
   if (int rc = lbrr_forward_chunk(e, e->dev_in, len, e->dev_out, e->stream)) return rc;
-  CK(cudaMemcpyAsync(e->pin_out, e->dev_out, out_b, cudaMemcpyDeviceToHost, e->stream));
+  const size_t slice = (out_b / kHostSlices + 255) / 256 * 256;
+  int slices = 0;
+  for (size_t o = 0; o < out_b; o += slice, ++slices) {
+    const size_t n = std::min(slice, out_b - o);
+    CK(cudaMemcpyAsync(reinterpret_cast<char*>(e->pin_out) + o, reinterpret_cast<const char*>(e->dev_out) + o, n,
+                       cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaEventRecord(e->host_ev[slices], e->stream));
+  }
+  const int workers = out_b < (4u << 20) ? 1 : 4;
+  std::atomic<int> copy_err{0};
+  auto copy_slices = [&](int w) {
+    for (int i = w; i < slices; i += workers) {
+      if (cudaEventSynchronize(e->host_ev[i]) != cudaSuccess) {
+        copy_err.store(1);
+        continue;
+      }
+      const size_t o = static_cast<size_t>(i) * slice;
+      std::memcpy(reinterpret_cast<char*>(outh) + o, reinterpret_cast<const char*>(e->pin_out) + o,
+                  std::min(slice, out_b - o));
+    }
+  };
+  std::vector<std::thread> th;
+  for (int w = 1; w < workers; ++w) th.emplace_back(copy_slices, w);
+  copy_slices(0);
+  for (auto& t : th) t.join();
   if (int rc = check_status(e->status, e->stream)) return rc;
-  std::memcpy(outh, e->pin_out, out_b);
+  if (copy_err.load()) return fail(LBRR_ERR_CUDA, "stem download");
   return LBRR_OK;
 }
 
