@@ -488,21 +488,44 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
     else
       store_2d(m, buf, c, t.row0 + rb, x.lane);
   };
-  (void)rows_valid;
-  // this thread's residual row, 32 columns at a time, loaded one chunk ahead
-  const float* rrow = (resid && valid) ? resid + static_cast<size_t>(my_row) * 256 : nullptr;
-  float4 rr[8], rn[8];
+  // The residual (dense rows only) is read 32 rows x 32 columns at a time,
+  // coalesced: 8 lanes per 128-byte row, 4 rows per instruction, one block
+  // ahead.  Each block goes through the warp's staging buffer, where every
+  // lane picks up its own row and then overwrites it with its output row.
+  const int rl = x.lane >> 3, vl = x.lane & 7;
+  const float* rbase = resid ? resid + static_cast<size_t>(t.row0 + rb) * 256 : nullptr;
+  float4 pre[8];
+  auto fetch = [&](int c) {
 #pragma unroll
-  for (int k = 0; k < 8; ++k) rr[k] = rrow ? *reinterpret_cast<const float4*>(rrow + c0 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + rl;
+      pre[it] = r < rows_valid ? ldg4(rbase + static_cast<size_t>(r) * 256 + c + 4 * vl) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (rbase) fetch(c0);
   float ss = 0.f;
 #pragma unroll 1
   for (int c = c0; c < c0 + kPartCols; c += 32) {
     const bool more = c + 32 < c0 + kPartCols;
-#pragma unroll
-    for (int k = 0; k < 8; ++k)
-      rn[k] = (rrow && more) ? *reinterpret_cast<const float4*>(rrow + c + 32 + 4 * k) : make_float4(0.f, 0.f, 0.f, 0.f);
     uint32_t v[32];
-    tmem_ld32(x.tm + c, v);
+    tmem_ld32(x.tm + c, v);  // in flight while the residual is staged
+    uint32_t* buf = x.st.f32_buf();
+    float4 rr[8];
+    if (rbase) {
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + rl;
+        *reinterpret_cast<float4*>(buf + r * 32 + ((vl ^ (r & 7)) << 2)) = pre[it];
+      }
+      if (more) fetch(c + 32);
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        rr[k] = *reinterpret_cast<const float4*>(buf + x.lane * 32 + ((k ^ (x.lane & 7)) << 2));
+    } else {
+#pragma unroll
+      for (int k = 0; k < 8; ++k) rr[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     tmem_ld_wait(v);
 #pragma unroll
     for (int j4 = 0; j4 < 8; ++j4) {
@@ -519,10 +542,7 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
       v[4 * j4 + 2] = __float_as_uint(o23.x);
       v[4 * j4 + 3] = __float_as_uint(o23.y);
     }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) rr[k] = rn[k];
-    uint32_t* buf = x.st.f32_buf();
-    stage_row<32>(buf, v, x.lane);
+    stage_row<32>(buf, v, x.lane);  // each lane rewrites only its own row
     store_out(&maps.out_map, buf, c);
     if (np.norm) tmem_st32(x.tm + c, v);
   }
