@@ -9,8 +9,9 @@
 // TMEM (TS-form MMA, V an MN-major shared-memory operand) and finish with
 // f16(f16(O / l) * sigmoid(gate)):
 //   attn_time_kernel  time axis, sequence = one band's T frames (a 3-D TMA box
-//                     gathers rows t*nb + b), two 128-row query tiles per CTA,
-//                     128-key tiles with an online softmax;
+//                     gathers rows t*nb + b), one 128-row query tile per CTA
+//                     and two CTAs per SM, 128-key tiles with an online
+//                     softmax;
 //   attn_freq_kernel  frequency axis, frames 2p and 2p+1 (62 bands each)
 //                     packed into one 128-row tile with a block-diagonal mask,
 //                     persistent CTAs walking (frame pair, head) items.
@@ -41,32 +42,29 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 // ---------------------------------------------------------------------------
-// Time axis: two query tiles per CTA, ping-pong between tensor core and softmax
+// Time axis: one query tile per CTA, two CTAs per SM
 // ---------------------------------------------------------------------------
-// One CTA (1 per SM, 384 threads) owns query tiles 2x and 2x+1 of one
-// (band, head) sequence; they share every K/V tile (4-stage TMA ring).  TMEM
-// (512 columns): S0 0..127, S1 128..255, O0 256..319, O1 320..383, P0
-// 384..447, P1 448..511.  Warpgroup 0 (warps 0..3) runs the softmax of slot
-// 0, warpgroup 1 (warps 4..7) that of slot 1, one query row per thread (warp
-// w reads TMEM lanes 32*(w%4)..); in warpgroup 2 warp 8 loads and warps 9
-// and 10 issue the MMAs of slots 0 and 1.  When slot s has written P_s(j), its
-// MMA warp issues O_s += P_s V_j and then S_s(j+2) into the S columns the
-// softmax has already read (S runs two key tiles ahead), so the softmax never
-// waits for its S.  The softmax warpgroups take 224 registers per thread from
-// warpgroup 2 (setmaxnreg), enough for a whole S row and its fp16 P without
-// spilling.
-constexpr int kT2Threads = 384;
-constexpr int kT2WarpTma = 8, kT2WarpMma = 9;  // warps 9 and 10 issue the MMAs of slots 0 and 1
-constexpr int kT2RegsSoftmax = 224, kT2RegsOther = 48;
-constexpr int kT2Stages = 4;
-constexpr int kT2OffQ = 0;
-constexpr int kT2OffKV = 2 * kTile;  // stage st: K at +2*st*kTile, V at +(2*st+1)*kTile
-constexpr int kT2OffBar = kT2OffKV + kT2Stages * 2 * kTile;
-constexpr int kT2Smem = kT2OffBar + 256;
-constexpr uint32_t kT2TmemCols = 512;
-__device__ __forceinline__ uint32_t t2_col_s(int slot) { return slot * 128u; }
-__device__ __forceinline__ uint32_t t2_col_o(int slot) { return 256u + slot * 64u; }
-__device__ __forceinline__ uint32_t t2_col_p(int slot) { return 384u + slot * 64u; }
+// One CTA (256 threads) owns one 128-row query tile of one (band, head)
+// sequence and streams its K/V tiles through a 3-stage TMA ring (3-D box for
+// the strided sequence).  Two CTAs share each SM (112 KB of shared memory and
+// 256 TMEM columns each): their softmax phases fall out of step, so one
+// CTA's exponentials run while the other loads S, stores P or waits for its
+// MMAs, and one CTA's start-up and epilogue overlap the other's work.  TMEM:
+// S 0..127, O 128..191, P 192..255.  Warps 0..3 run the softmax, one query
+// row per thread (warp w reads TMEM lanes 32w..); warp 4 loads, warp 5
+// issues the MMAs.  S runs two key tiles ahead of the softmax: once the
+// softmax holds S(j+1) in registers, the issuer computes S(j+2) into the same
+// columns, right after O += P(j)·V(j) (TS form, A = P from TMEM).  The
+// softmax warpgroup takes 224 registers per thread from warpgroup 1
+// (setmaxnreg), enough for a whole S row and its fp16 P without spilling.
+constexpr int kT1Threads = 256;
+constexpr int kT1WarpTma = 4, kT1WarpMma = 5;
+constexpr int kT1RegsSoftmax = 224, kT1RegsOther = 32;
+constexpr int kT1Stages = 3;
+constexpr int kT1OffQ = 0;
+constexpr int kT1OffKV = kTile;  // stage st: K at +2*st*kTile, V at +(2*st+1)*kTile
+constexpr int kT1OffBar = kT1OffKV + kT1Stages * 2 * kTile;
+constexpr int kT1Smem = kT1OffBar + 128;
 
 __device__ __forceinline__ float max3f(float a, float b, float c) {
   float r;
@@ -74,18 +72,19 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return r;
 }
 
-__global__ void __launch_bounds__(kT2Threads, 1)
+__global__ void __launch_bounds__(kT1Threads, 2)
     attn_time_kernel(const __grid_constant__ CUtensorMap tm, const AttnArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT2OffBar);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kT1OffBar);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;    // [kT2Stages]
-  uint64_t* kv_empty = bars + 5;   // [kT2Stages]
-  uint64_t* s_full = bars + 9;     // [2]
-  uint64_t* p_full = bars + 11;    // [2]
-  uint64_t* s_free = bars + 13;    // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  uint64_t* kv_full = bars + 1;   // [kT1Stages]
+  uint64_t* kv_empty = bars + 4;  // [kT1Stages]
+  uint64_t* s_full = bars + 7;    // phase j: S(j) written
+  uint64_t* o_done = bars + 8;    // phase j: O += P(j) V(j) done
+  uint64_t* p_full = bars + 9;    // phase j: P(j) written (128 softmax threads)
+  uint64_t* s_free = bars + 10;   // phase j: S(j) read into registers
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   if ((smem_u32(smem) & 1023u) != 0) {
@@ -94,75 +93,67 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   }
   const int nb = a.nb, T = a.T, nk = a.nk;
   const int head = blockIdx.y & 7, band = blockIdx.y >> 3;
-  const int qt0 = blockIdx.x * 2;
-  const int nslots = (qt0 + 1) * 128 < T ? 2 : 1;
+  const int qt = blockIdx.x;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kT2Stages; ++i) {
+    for (int i = 0; i < kT1Stages; ++i) {
       mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], nslots);  // one commit per slot's MMA issuer
+      mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&s_free[i], 128);
-    }
+    mbar_init(s_full, 1);
+    mbar_init(o_done, 1);
+    mbar_init(p_full, 128);
+    mbar_init(s_free, 128);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == kT2WarpTma && lane == 0) tma_prefetch(&tm);
-  if (warp == kT2WarpMma) {
-    tmem_alloc(tmem_slot, kT2TmemCols);
+  if (warp == kT1WarpTma && lane == 0) tma_prefetch(&tm);
+  if (warp == kT1WarpMma) {
+    tmem_alloc(tmem_slot, kAttnTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // Register split, 2 x 128 x 224 + 128 x 48 <= 384 x 168 launch registers
-  // (the launcher checks the compiled count before the first launch); each
-  // role changes its own warpgroup's count at the top of its branch.
-  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kT2RegsOther));
-  if (warp == kT2WarpTma) {
+  // Register split, 128 x 224 + 128 x 32 <= 256 x 128 launch registers (two
+  // CTAs per SM; the launcher checks the compiled count before the first
+  // launch); each role changes its own warpgroup's count at the top of its
+  // branch.
+  if (warp >= 4) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kT1RegsOther));
+  if (warp == kT1WarpTma) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, nslots * kTile);
-      for (int s = 0; s < nslots; ++s)
-        tma_load_3d(smem + kT2OffQ + s * kTile, &tm, q_full, head * 64, band, (qt0 + s) * 128);
+      mbar_arrive_expect_tx(q_full, kTile);
+      tma_load_3d(smem + kT1OffQ, &tm, q_full, head * 64, band, qt * 128);
       for (int j = 0; j < nk; ++j) {
-        const int st = j % kT2Stages;
-        if (!mbar_wait(&kv_empty[st], ((j / kT2Stages) & 1) ^ 1u, abort_flag, a.status)) break;
+        const int st = j % kT1Stages;
+        if (!mbar_wait(&kv_empty[st], ((j / kT1Stages) & 1) ^ 1u, abort_flag, a.status)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
-        uint8_t* kv = smem + kT2OffKV + st * 2 * kTile;
+        uint8_t* kv = smem + kT1OffKV + st * 2 * kTile;
         tma_load_3d(kv, &tm, &kv_full[st], 512 + head * 64, band, j * 128);
         tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, j * 128);
       }
     }
-  } else if (warp == kT2WarpMma || warp == kT2WarpMma + 1) {
-    // ---------------- MMA issuers, one per slot ----------------
-    // tcgen05.mma issue blocks while the tensor pipe is busy, so each slot has
-    // its own issuing thread: one slot's waits overlap the other's MMAs.
-    // s_full[s] completes phase 0 with S_s(0), phase 1 with S_s(1), and phase
-    // j+2 with O_s += P_s(j) V_j together with S_s(j+2): S runs two key tiles
-    // ahead of the softmax, PV one behind.
-    const int s = warp - kT2WarpMma;
-    if (lane == 0 && s < nslots) {
+  } else if (warp == kT1WarpMma) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
       const uint32_t id_s = idesc_f16_f32(128, 128);
       const uint32_t id_o = idesc_f16_f32(128, 64, /*b_mn_major=*/true);
-      const uint32_t sq = smem_u32(smem + kT2OffQ + s * kTile);
+      const uint32_t sq = smem_u32(smem + kT1OffQ);
       auto issue_s = [&](int st) {
-        const uint32_t sk = smem_u32(smem + kT2OffKV + st * 2 * kTile);
+        const uint32_t sk = smem_u32(smem + kT1OffKV + st * 2 * kTile);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tmem + t2_col_s(s), sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
+          mma_f16_ss(tmem + kColS, sdesc_sw128(sq + k * 32, 1024, 16), sdesc_sw128(sk + k * 32, 1024, 16), id_s,
                      k > 0 ? 1u : 0u);
       };
       auto issue_pv = [&](int st, bool acc) {
-        const uint32_t sv = smem_u32(smem + kT2OffKV + (st * 2 + 1) * kTile);
+        const uint32_t sv = smem_u32(smem + kT1OffKV + (st * 2 + 1) * kTile);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_f16_ts(tmem + t2_col_o(s), tmem + t2_col_p(s) + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
+          mma_f16_ts(tmem + kColO, tmem + kColP + kk * 8, sdesc_sw128(sv + kk * 2048, 1024, 0), id_o,
                      (acc || kk > 0) ? 1u : 0u);
       };
       bool ok = mbar_wait(q_full, 0, abort_flag, a.status);
@@ -170,49 +161,53 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       if (ok) {
         tc_fence_after();
         issue_s(0);
-        mma_commit(&s_full[s]);
+        mma_commit(s_full);
         if (nk > 1) {
-          ok = mbar_wait(&kv_full[1], 0, abort_flag, a.status);
-          if (ok) ok = mbar_wait(&s_free[s], 0, abort_flag, a.status);
+          ok = mbar_wait(&kv_full[1 % kT1Stages], 0, abort_flag, a.status);
+          if (ok) ok = mbar_wait(s_free, 0, abort_flag, a.status);
           if (ok) {
             tc_fence_after();
-            issue_s(1);
+            issue_s(1 % kT1Stages);
+            mma_commit(s_full);
           }
         }
-        if (ok) mma_commit(&s_full[s]);
       }
       for (int j = 0; ok && j < nk; ++j) {
-        ok = mbar_wait(&p_full[s], j & 1, abort_flag, a.status);
+        ok = mbar_wait(p_full, j & 1, abort_flag, a.status);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(j % kT2Stages, j > 0);
+        issue_pv(j % kT1Stages, j > 0);
+        mma_commit(o_done);
+        mma_commit(&kv_empty[j % kT1Stages]);
         if (j + 2 < nk) {
-          const int st2 = (j + 2) % kT2Stages;
-          ok = mbar_wait(&kv_full[st2], ((j + 2) / kT2Stages) & 1, abort_flag, a.status);
-          if (ok) ok = mbar_wait(&s_free[s], (j + 1) & 1, abort_flag, a.status);
+          const int st2 = (j + 2) % kT1Stages;
+          ok = mbar_wait(&kv_full[st2], ((j + 2) / kT1Stages) & 1, abort_flag, a.status);
+          if (ok) ok = mbar_wait(s_free, (j + 1) & 1, abort_flag, a.status);
           if (!ok) break;
           tc_fence_after();
           issue_s(st2);
+          mma_commit(s_full);
         }
-        mma_commit(&s_full[s]);
-        mma_commit(&kv_empty[j % kT2Stages]);
       }
     }
-  } else if (warp < 8) {
+  } else if (warp < 4) {
     // ---------------- softmax + epilogue (one query row per thread) ----------------
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kT2RegsSoftmax));
-    const int slot = warp >> 2;
-    const int q = warp & 3;
-    const int r = q * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-    const uint32_t tS = tmem + lane_off + t2_col_s(slot);
-    const uint32_t tO = tmem + lane_off + t2_col_o(slot);
-    const uint32_t tP = tmem + lane_off + t2_col_p(slot);
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kT1RegsSoftmax));
+    const int r = warp * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tS = tmem + lane_off + kColS;
+    const uint32_t tO = tmem + lane_off + kColO;
+    const uint32_t tP = tmem + lane_off + kColP;
+    const int qi = qt * 128 + r;
+    const bool valid = qi < T;
+    const int token = qi * nb + band;
+    // the gate is needed only in the epilogue; its load latency hides here
+    const float gate = valid ? __ldg(a.gates + static_cast<size_t>(token) * 8 + head) : 0.f;
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
     float m_run = -INFINITY, l_run = 0.f;
-    bool ok = slot < nslots;
+    bool ok = true;
     for (int j = 0; ok && j < nk; ++j) {
-      ok = mbar_wait(&s_full[slot], j & 1, abort_flag, a.status);
+      ok = mbar_wait(s_full, j & 1, abort_flag, a.status);
       if (!ok) break;
       tc_fence_after();
       const int hi = min(128, T - j * 128);  // valid keys of this tile: [0, hi)
@@ -223,7 +218,7 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       for (int q4 = 0; q4 < 4; ++q4) tmem_ld_wait(s[q4]);
       // S is in registers: the MMA warp may overwrite it with the next tile
       tc_fence_before();
-      mbar_arrive(&s_free[slot]);
+      mbar_arrive(s_free);
       if (hi < 128) {
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4)
@@ -274,9 +269,9 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
       const float sum = sa.x + sa.y;
       if (j > 0) {
-        // O_s += P V_{j-1} (phase j+1) must be complete before O is rescaled
-        // and P rewritten
-        ok = mbar_wait(&s_full[slot], (j + 1) & 1, abort_flag, a.status);
+        // O += P(j-1) V(j-1) must be complete before O is rescaled and P
+        // rewritten
+        ok = mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status);
         if (!ok) break;
         tc_fence_after();
         if (__any_sync(0xffffffffu, corr != 1.0f)) {
@@ -303,20 +298,14 @@ __global__ void __launch_bounds__(kT2Threads, 1)
       l_run = l_run * corr + sum;
       m_run = m_next;
       tc_fence_before();
-      mbar_arrive(&p_full[slot]);
+      mbar_arrive(p_full);
     }
-    // last PV: phase nk+1 (with a single key tile, phase 1 is passed first so
-    // that the parity wait never runs two phases behind)
-    if (ok && nk == 1) ok = mbar_wait(&s_full[slot], 1, abort_flag, a.status);
-    if (ok) ok = mbar_wait(&s_full[slot], (nk + 1) & 1, abort_flag, a.status);
+    // last PV
+    if (ok) ok = mbar_wait(o_done, (nk - 1) & 1, abort_flag, a.status);
     tc_fence_after();
     if (ok && !*abort_flag) {
-      const int qi = (qt0 + slot) * 128 + r;
-      const bool valid = qi < T;
-      const int token = qi * nb + band;
       const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      float sig = 0.f;
-      if (valid) sig = 1.0f / (1.0f + __expf(-__ldg(a.gates + static_cast<size_t>(token) * 8 + head)));
+      const float sig = valid ? 1.0f / (1.0f + __expf(-gate)) : 0.f;
 #pragma unroll 1
       for (int c = 0; c < 64; c += 32) {
         uint32_t v[32];
@@ -340,9 +329,9 @@ __global__ void __launch_bounds__(kT2Threads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kT2WarpMma) {
+  if (warp == kT1WarpMma) {
     tc_fence_after();
-    tmem_dealloc(tmem, kT2TmemCols);
+    tmem_dealloc(tmem, kAttnTmemCols);
   }
 }
 // ---------------------------------------------------------------------------
@@ -559,14 +548,14 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   cudaError_t ce = once_per_device(configured, [] {
     cudaError_t e = cudaFuncSetAttribute(attn_freq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kT2Smem);
+      e = cudaFuncSetAttribute(attn_time_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kT1Smem);
     if (e != cudaSuccess) return e;
     // setmaxnreg.inc waits until the block's launch registers cover the split;
     // refuse to launch a build whose register count would not
     cudaFuncAttributes fa;
     e = cudaFuncGetAttributes(&fa, attn_time_kernel);
     if (e != cudaSuccess) return e;
-    if (fa.numRegs * kT2Threads < 2 * 128 * kT2RegsSoftmax + 128 * kT2RegsOther) return cudaErrorInvalidConfiguration;
+    if (fa.numRegs * kT1Threads < 128 * kT1RegsSoftmax + 128 * kT1RegsOther) return cudaErrorInvalidConfiguration;
     return cudaSuccess;
   });
   if (ce != cudaSuccess) return ce;
@@ -585,8 +574,8 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     e = make_map_3d(&tm, qkv, 1536, nb, T, 1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
     if (e != cudaSuccess) return e;
     a.nk = (T + 127) / 128;
-    // two query tiles per CTA
-    attn_time_kernel<<<dim3((a.nk + 1) / 2, nb * 8), kT2Threads, kT2Smem, st>>>(tm, a);
+    // one query tile per CTA, two CTAs per SM
+    attn_time_kernel<<<dim3(a.nk, nb * 8), kT1Threads, kT1Smem, st>>>(tm, a);
     return cudaGetLastError();
   }
   e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
