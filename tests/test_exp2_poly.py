@@ -1,5 +1,5 @@
 """The polynomial exp2 of the attention softmax (csrc/exp2_poly.cuh) against
-its error bound: the device sequence (clamp, magic-number rounding, degree-5
+its error bound: the device sequence (clamp, magic-number rounding, degree-4
 polynomial in fp32 FMAs, exponent-field add) is replayed here in numpy fp32
 and compared with the exact 2^x.  The coefficients in the header must be the
 ones csrc/exp2_poly.py (Remez fit) produces."""
@@ -40,8 +40,8 @@ def exp2_poly_replay(x):
     t = (x + rnd).astype(np.float32)
     j = (t - rnd).astype(np.float32)
     f = fma32(j, f32(-1.0), x)
-    p = fma32(f32(c[5]), f, f32(c[4]))
-    for k in (3, 2, 1, 0):
+    p = fma32(f32(c[-1]), f, f32(c[-2]))
+    for k in range(len(c) - 3, -1, -1):
         p = fma32(p, f, f32(c[k]))
     bits = p.view(np.int32).astype(np.int64) + ((t.view(np.int32).astype(np.int64) << 23) & 0xFFFFFFFF)
     return (bits & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
@@ -51,9 +51,9 @@ def test_header_matches_fit():
     m = _fit_module()
     got = header_coefficients()
     want = m.coefficients_f32()
-    assert len(got) == 6
+    assert len(got) == 5
     assert np.array_equal(np.array(got, np.float32), want)
-    assert m.max_rel_error(want) < 2e-7
+    assert m.max_rel_error(want) < 3e-6
 
 
 def test_relative_error_bound():
@@ -64,7 +64,7 @@ def test_relative_error_bound():
     got = exp2_poly_replay(x).astype(np.float64)
     want = np.exp2(x.astype(np.float64))
     rel = np.abs(got / want - 1.0)
-    assert rel.max() < 4e-7, rel.max()
+    assert rel.max() < 3.2e-6, rel.max()
 
 
 def test_clamp_and_fp16_rounding():
@@ -73,4 +73,4 @@ def test_clamp_and_fp16_rounding():
     assert np.all(np.isfinite(y))
     assert np.all(y[:4] <= np.float32(2.0 ** -125))
     assert np.all(y[:4].astype(np.float16) == 0)
-    assert abs(float(y[4]) - 1.0) < 2e-7 and abs(float(y[5]) / 256.0 - 1.0) < 2e-7
+    assert abs(float(y[4]) - 1.0) < 3e-6 and abs(float(y[5]) / 256.0 - 1.0) < 3e-6
