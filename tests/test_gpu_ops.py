@@ -81,6 +81,29 @@ def test_attention(lb, T, axis):
     assert snr_db(got, ref) > 55.0, snr_db(got, ref)
 
 
+def test_attention_max_jump(lb):
+    """Time axis: keys of the second and third key tiles score far above the
+    first tile's, so the row max grows by more than 2^8 in exp2 units mid-row
+    (enough to overflow an fp16 P against the old max): the kernel must raise
+    its reference max, rescale O and recompute those tiles' P."""
+    T = 300
+    M = T * NB
+    qkv = randn((M, 1536), 33, 1.0)
+    frame = torch.arange(M) // NB  # token = t * nb + b
+    k = qkv[:, 512:1024]
+    k[(frame >= 128) & (frame < 160)] *= 12.0
+    k[frame >= 256] *= 30.0
+    qkv = f16(qkv)
+    gates = randn((M, 8), 34, 1.0)
+    out = torch.empty(M, 512, dtype=torch.float16, device="cuda")
+    lb.attention(cuda(qkv, torch.float16), cuda(gates), out, T, NB, 0)
+    lb.op_sync()
+    ref = oracle_attention_gated(qkv, gates, T, NB, 0)
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert snr_db(got, ref) > 55.0, snr_db(got, ref)
+
+
 @pytest.mark.parametrize("M", [62, 2294, 16058])
 def test_outproj_norm(lb, M):
     s = f16(randn((M, 512), 30, 0.5))
