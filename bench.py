@@ -45,9 +45,9 @@ SONG_LEN = 7959168  # 180.48 s at 44.1 kHz
 SR = 44100
 METRIC = "ms/588800-sample chunk"
 # this repository's kernels per chunk forward: frames, band_norm, band-split GEMM,
-# 24 x (QKV, attention, out-proj, FF1, FF2), mask GEMM1, mask GEMM2, ISTFT
+# 24 x (QKV, attention, out-proj, fused FF), mask GEMM1, mask GEMM2, ISTFT
 # (the two cuFFT executions are library kernels and not counted)
-LAUNCHES_PER_CHUNK = 3 + 24 * 5 + 3
+LAUNCHES_PER_CHUNK = 3 + 24 * 4 + 3
 UNIT = "ms/chunk"
 
 
@@ -485,6 +485,14 @@ def run_op(args):
             b = torch.zeros(1024, device="cuda")
             o = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
             fn = lambda: lbrr.ff1_gelu(h, w, b, o)  # noqa: E731
+        elif args.op == "ff":
+            w1 = (torch.randn(1024, 256, device="cuda", generator=g) * 0.02).half()
+            b1 = torch.zeros(1024, device="cuda")
+            w2 = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
+            b2 = torch.zeros(256, device="cuda")
+            r = torch.randn(M, 256, device="cuda", generator=g)
+            o = torch.empty(M, 256, device="cuda")
+            fn = lambda: lbrr.feed_forward(h, w1, b1, w2, b2, r, o)  # noqa: E731
         elif args.op == "ff2":
             f = torch.randn(M, 1024, device="cuda", generator=g).half()
             w = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
@@ -521,7 +529,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--forward-only", action="store_true", help="profiling: chunk forwards only")
-    ap.add_argument("--op", choices=["attn_time", "attn_freq", "qkv", "outproj", "ff1", "ff2"],
+    ap.add_argument("--op", choices=["attn_time", "attn_freq", "qkv", "outproj", "ff1", "ff2", "ff"],
                     help="profiling: run one kernel")
     ap.add_argument("--frames", type=int, default=0, help="profiling: frames T (default 1151)")
     args = ap.parse_args()

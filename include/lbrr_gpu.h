@@ -194,6 +194,13 @@ int lbrr_op_ff1_gelu(const uint16_t* h16, const uint16_t* w16, const float* b1, 
 int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const float* b2, const float* resid, float* x,
                       int64_t rows, void* stream);
 
+/* Feed-forward in one kernel: x = FF2(f16(gelu(FF1(h16) + b1))) + b2 + resid,
+ * the same values as lbrr_op_ff1_gelu followed by lbrr_op_ff2_resid
+ * (src/main.rs:6234-6259) without the [rows][1024] fp16 intermediate in
+ * device memory.  w1_16 [1024][256], w2_16 [256][1024] fp16. */
+int lbrr_op_feed_forward(const uint16_t* h16, const uint16_t* w1_16, const float* b1, const uint16_t* w2_16,
+                         const float* b2, const float* resid, float* x, int64_t rows, void* stream);
+
 int lbrr_op_sync(void* stream);
 
 /* Feed-forward half of a RoFormer step (FF1 + GELU, then FF2 + bias +

@@ -178,7 +178,7 @@ struct lbrr_engine {
   size_t sarena_bytes = 0;
   float *window = nullptr, *frames = nullptr, *x = nullptr, *gates = nullptr, *attn_out = nullptr, *pcm = nullptr;
   float2 *spec = nullptr, *c2r = nullptr;
-  __half *xn = nullptr, *h16 = nullptr, *qkv = nullptr, *scaled = nullptr, *ff1 = nullptr, *xb16 = nullptr,
+  __half *xn = nullptr, *h16 = nullptr, *qkv = nullptr, *scaled = nullptr, *xb16 = nullptr,
          *hidden = nullptr;
   int* status = nullptr;
   // host staging for the end-to-end entry point
@@ -340,7 +340,7 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   const size_t o_win = s.take<float>(kNfft), o_fr = s.take<float>(2 * T * kNfft), o_sp = s.take<float2>(2 * T * kBins);
   const size_t o_xn = s.take<__half>(T * G.xn_cols), o_x = s.take<float>(M * 256), o_h = s.take<__half>(M * 256);
   const size_t o_g = s.take<float>(M * 8), o_qkv = s.take<__half>(M * 1536), o_sc = s.take<__half>(M * 512);
-  const size_t o_ao = s.take<float>(M * 256), o_ff = s.take<__half>(M * 1024), o_xb = s.take<__half>(M * 256);
+  const size_t o_ao = s.take<float>(M * 256), o_xb = s.take<__half>(M * 256);
   const size_t o_hid = s.take<__half>(static_cast<size_t>(kStems) * M * 1024);
   const size_t o_c2r = s.take<float2>(static_cast<size_t>(2 * kStems) * T * kBins);
   const size_t o_pcm = s.take<float>(static_cast<size_t>(2 * kStems) * T * kNfft);
@@ -378,7 +378,6 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   e->qkv = reinterpret_cast<__half*>(S + o_qkv);
   e->scaled = reinterpret_cast<__half*>(S + o_sc);
   e->attn_out = reinterpret_cast<float*>(S + o_ao);
-  e->ff1 = reinterpret_cast<__half*>(S + o_ff);
   e->xb16 = reinterpret_cast<__half*>(S + o_xb);
   e->hidden = reinterpret_cast<__half*>(S + o_hid);
   e->c2r = reinterpret_cast<float2*>(S + o_c2r);
@@ -775,7 +774,6 @@ static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
                e->qkv, M, kNumBands, axis, e->status, st));
   CKL(attention_fwd(e->qkv, e->gates, e->scaled, T, kNumBands, axis, e->status, st));
   CKL(gemm_outproj_norm(e->scaled, w.wo, e->out_bias, e->x, w.ff_g, e->attn_out, e->h16, M, e->status, st));
-  CKL(gemm_ff1_gelu(e->h16, w.w1, w.b1, e->ff1, M, e->status, st));
   RowNorm next;
   if (k + 1 < 2 * kDepth) {
     next = attn_norm(e, k + 1);
@@ -786,7 +784,8 @@ static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
     next.T = T;
     next.nb = kNumBands;
   }
-  CKL(gemm_ff2_resid(e->ff1, w.w2, w.b2, e->attn_out, e->x, M, next, e->status, st));
+  // FF1 -> GELU -> FF2 + residual, the hidden activation kept on chip
+  CKL(gemm_ff_fused(e->h16, w.w1, w.b1, w.w2, w.b2, e->attn_out, e->x, M, next, e->status, st));
   return LBRR_OK;
 }
 
@@ -1521,6 +1520,18 @@ extern "C" int lbrr_op_ff2_resid(const uint16_t* ff1, const uint16_t* w16, const
   OP_PROLOGUE
   CK(gemm_ff2_resid(reinterpret_cast<const __half*>(ff1), reinterpret_cast<const __half*>(w16), b2, resid, x,
                     static_cast<int>(rows), RowNorm(), status, st));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_op_feed_forward(const uint16_t* h16, const uint16_t* w1_16, const float* b1,
+                                    const uint16_t* w2_16, const float* b2, const float* resid, float* x,
+                                    int64_t rows, void* stream) {
+  if (!h16 || !w1_16 || !b1 || !w2_16 || !b2 || !resid || !x || rows <= 0 || rows > (1ll << 30))
+    return fail(LBRR_ERR_INVALID, "lbrr_op_feed_forward: bad arguments");
+  OP_PROLOGUE
+  CK(gemm_ff_fused(reinterpret_cast<const __half*>(h16), reinterpret_cast<const __half*>(w1_16), b1,
+                   reinterpret_cast<const __half*>(w2_16), b2, resid, x, static_cast<int>(rows), RowNorm(), status,
+                   st));
   return LBRR_OK;
 }
 

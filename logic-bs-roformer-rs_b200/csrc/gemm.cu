@@ -4,7 +4,7 @@
 // D = A[128 x K] * B[n x K]^T with fp16 operands (both K-major, 128-byte
 // swizzled, fed by TMA) and an fp32 accumulator in TMEM.  One CTA per SM
 // walks the tile list with a static stride.  Warp roles (64 + 32 * kEpiWarps threads):
-//   warp 0      TMA producer (one lane): 4-stage ring of 48 KB (A 16 KB + B 32 KB)
+//   warp 0      TMA producer (one lane): 3-stage ring of 48 KB (A 16 KB + B 32 KB)
 //   warp 1      TMEM allocator (all 512 columns) + single-thread tcgen05.mma
 //               issuer into two 256-column accumulators (double buffer)
 //   warps 2..9  epilogue: two warps per TMEM lane quadrant, each owning 128 of
@@ -882,6 +882,326 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// Fused feed-forward: x = W2 f16(gelu(W1 h + b1)) + b2 + resid, then the row
+// epilogue (next RMSNorm); the [M][1024] hidden activation never leaves the SM
+// ---------------------------------------------------------------------------
+// Per 128-row tile, FF1 runs in 4 chunks of 256 hidden units into a
+// 256-column TMEM accumulator (acc1, columns 0..255).  The epilogue warps load
+// a chunk into registers (which frees acc1 for the next chunk's FF1), turn it
+// into f16(gelu(acc + b1)) (the values the unfused FF1 stores) and write it
+// into shared memory as FF2's A operand G (K-major, 128-byte swizzle, four
+// [128][64] tiles).  FF2 accumulates chunk by chunk into a second 256-column
+// accumulator (acc2, columns 256..511) in the same K order as the unfused
+// FF2; after the last chunk the epilogue warps run the N = 256 row epilogue,
+// whose staging buffers reuse G.  All MMAs are
+// 128 x 256 x 16 (an N = 128 MMA would read as many shared-memory bytes per
+// FLOP as the SM can deliver).
+// MMA order per tile: FF1(0), FF1(1), FF2(0), FF1(2), FF2(1), FF1(3),
+// FF2(2), FF2(3), so each chunk's GELU overlaps the next chunk's FF1 and the
+// previous chunk's FF2.  The weights stream through a 2-stage ring of 32 KB
+// tiles ([256][64] fp16) in that order: W1 chunk c and W2 chunk c are 4
+// K-blocks each.  Warps: 0..7 epilogue (two per TMEM lane quadrant, 128 of
+// the 256 columns each), 8 weight loads, 9 TMEM allocation + MMA issue, 10
+// h-tile loads (one [128][256] tile per 128 rows, reloaded once the tile's
+// FF1 is done).  The epilogue warpgroups take 200 registers per thread and
+// warpgroup 2 keeps 104 (setmaxnreg): a whole 128-column chunk row and its
+// fp16 pairs fit without spilling.
+constexpr int kFfChunk = 256;
+constexpr int kFfChunks = 1024 / kFfChunk;
+constexpr int kFfTileBytes = kBM * kBK * 2;   // 16 KB: [128][64] fp16
+constexpr int kFfWBytes = kFfChunk * kBK * 2;  // 32 KB: [256][64] fp16
+constexpr int kFfWStages = 2;
+constexpr int kFfOffH = 0;                           // 4 tiles (K = 256)
+constexpr int kFfOffG = kFfOffH + 4 * kFfTileBytes;  // 4 tiles (K = 256 hidden units of a chunk)
+constexpr int kFfOffW = kFfOffG + 4 * kFfTileBytes;  // weight ring
+constexpr int kFfOffConst = kFfOffW + kFfWStages * kFfWBytes;
+constexpr int kFfConstFloats = 4096;
+constexpr int kFfB1 = 3072;  // b1 in the constants region, after the row epilogue's constants
+constexpr int kFfOffBar = kFfOffConst + kFfConstFloats * 4;
+constexpr int kFfSmem = kFfOffBar + 256;
+constexpr int kFfThreads = kEpiWarps * 32 + 128;
+constexpr int kFfWarpW = kEpiWarps, kFfWarpMma = kEpiWarps + 1, kFfWarpH = kEpiWarps + 2;
+constexpr int kFfRegsEpi = 200, kFfRegsOther = 104;
+static_assert(kFfSmem <= 232448, "exceeds the 227 KB per-CTA shared memory limit");
+static_assert(kRowGateB + 8 <= kFfB1 && kFfB1 + 1024 <= kFfConstFloats, "constants overlap");
+static_assert(kEpiWarps * kStageWords * 4 <= 4 * kFfTileBytes, "staging must fit in G");
+static_assert(kEpiWarps == 8 && kPartCols == 128, "two epilogue warps per quadrant, 128 columns each");
+
+__global__ void __launch_bounds__(kFfThreads, 1)
+    ff_fused_kernel(const __grid_constant__ CUtensorMap tmH, const __grid_constant__ CUtensorMap tmW1,
+                    const __grid_constant__ CUtensorMap tmW2, const __grid_constant__ EpiRow256 epi,
+                    const float* b1, int n_tiles, int* status) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kFfOffBar);
+  uint64_t* w_full = bars;                  // [kFfWStages]
+  uint64_t* w_empty = w_full + kFfWStages;  // [kFfWStages]
+  uint64_t* h_full = w_empty + kFfWStages;
+  uint64_t* h_empty = h_full + 1;
+  uint64_t* a1_full = h_empty + 1;   // FF1 chunk in acc1
+  uint64_t* a1_empty = a1_full + 1;  // acc1 loaded by every epilogue warp
+  uint64_t* g_full = a1_empty + 1;   // G written
+  uint64_t* g_empty = g_full + 1;    // G consumed by FF2
+  uint64_t* a2_full = g_empty + 1;
+  uint64_t* a2_empty = a2_full + 1;
+  uint64_t* stage_free = a2_empty + 1;  // every epilogue warp's row-epilogue stores have read G
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(stage_free + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) report_status(status, kDevSmemMisaligned);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFfWStages; ++s) {
+      mbar_init(&w_full[s], 1);
+      mbar_init(&w_empty[s], 1);
+    }
+    mbar_init(h_full, 1);
+    mbar_init(h_empty, 1);
+    mbar_init(a1_full, 1);
+    mbar_init(a1_empty, kEpiWarps);
+    mbar_init(g_full, kEpiWarps);
+    mbar_init(g_empty, 1);
+    mbar_init(a2_full, 1);
+    mbar_init(a2_empty, kEpiWarps);
+    mbar_init(stage_free, kEpiWarps);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == kFfWarpW && lane == 0) {
+    tma_prefetch(&tmW1);
+    tma_prefetch(&tmW2);
+  }
+  if (warp == kFfWarpH && lane == 0) tma_prefetch(&tmH);
+  if (warp == kFfWarpMma) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Register split, 256 x 200 + 128 x 104 <= 384 x 168 launch registers (the
+  // launcher checks the compiled count before the first launch); each role
+  // changes its own warpgroup's count at the top of its branch.
+  if (warp >= kEpiWarps) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kFfRegsOther));
+
+  if (warp == kFfWarpW) {
+    // ---------------- weight tiles, in MMA order ----------------
+    if (lane == 0) {
+      uint32_t wc = 0;
+      bool ok = true;
+      auto load_w = [&](const CUtensorMap* m, int x, int y) {
+        const int s = wc % kFfWStages;
+        const uint32_t ph = (wc / kFfWStages) & 1;
+        ++wc;
+        if (!(ok = mbar_wait(&w_empty[s], ph ^ 1u, abort_flag, status))) return;
+        mbar_arrive_expect_tx(&w_full[s], kFfWBytes);
+        tma_load_2d(smem + kFfOffW + s * kFfWBytes, m, &w_full[s], x, y);
+      };
+      auto load_w1 = [&](int c) {
+        for (int kb = 0; ok && kb < 4; ++kb) load_w(&tmW1, kb * kBK, c * kFfChunk);
+      };
+      auto load_w2 = [&](int c) {
+        for (int kb = 0; ok && kb < 4; ++kb) load_w(&tmW2, c * kFfChunk + kb * kBK, 0);
+      };
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        for (int c = 0; ok && c < kFfChunks; ++c) {
+          load_w1(c);
+          if (c > 0) load_w2(c - 1);
+        }
+        if (ok) load_w2(kFfChunks - 1);
+      }
+    }
+  } else if (warp == kFfWarpH) {
+    // ---------------- h tiles ----------------
+    if (lane == 0) {
+      int i = 0;
+      for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++i) {
+        if (!mbar_wait(h_empty, (i & 1) ^ 1u, abort_flag, status)) break;
+        mbar_arrive_expect_tx(h_full, 4 * kFfTileBytes);
+        for (int kb = 0; kb < 4; ++kb)
+          tma_load_2d(smem + kFfOffH + kb * kFfTileBytes, &tmH, h_full, kb * kBK, tile * kBM);
+      }
+    }
+  } else if (warp == kFfWarpMma) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t wc = 0;
+      const uint32_t id = idesc_f16_f32(kBM, kFfChunk);
+      auto w_tile = [&](uint32_t& sb) {
+        const int s = wc % kFfWStages;
+        if (!mbar_wait(&w_full[s], (wc / kFfWStages) & 1, abort_flag, status)) return false;
+        tc_fence_after();
+        sb = smem_u32(smem + kFfOffW + s * kFfWBytes);
+        return true;
+      };
+      auto w_release = [&]() {
+        mma_commit(&w_empty[wc % kFfWStages]);
+        ++wc;
+      };
+      // g: chunk index over this CTA's tiles (phase g of the chunk barriers)
+      auto ff1 = [&](int g) {
+        if (!mbar_wait(a1_empty, (g & 1) ^ 1u, abort_flag, status)) return false;
+        tc_fence_after();
+        for (int kb = 0; kb < 4; ++kb) {
+          uint32_t sb;
+          if (!w_tile(sb)) return false;
+          const uint32_t sa = smem_u32(smem + kFfOffH + kb * kFfTileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_ss(tmem, sdesc_sw128(sa + k * 32, 1024, 16), sdesc_sw128(sb + k * 32, 1024, 16), id,
+                       (kb | k) != 0 ? 1u : 0u);
+          w_release();
+        }
+        mma_commit(a1_full);
+        return true;
+      };
+      auto ff2 = [&](int g, int c, int i) {
+        if (c == 0) {
+          if (!mbar_wait(a2_empty, (i & 1) ^ 1u, abort_flag, status)) return false;
+        }
+        if (!mbar_wait(g_full, g & 1, abort_flag, status)) return false;
+        tc_fence_after();
+        for (int kb = 0; kb < 4; ++kb) {
+          uint32_t sb;
+          if (!w_tile(sb)) return false;
+          const uint32_t sa = smem_u32(smem + kFfOffG + kb * kFfTileBytes);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k)
+            mma_f16_ss(tmem + kFfChunk, sdesc_sw128(sa + k * 32, 1024, 16), sdesc_sw128(sb + k * 32, 1024, 16), id,
+                       (c | kb | k) != 0 ? 1u : 0u);
+          w_release();
+        }
+        mma_commit(g_empty);
+        return true;
+      };
+      bool ok = true;
+      int i = 0;
+      for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++i) {
+        if (!(ok = mbar_wait(h_full, i & 1, abort_flag, status))) break;
+        tc_fence_after();
+        const int g0 = i * kFfChunks;
+        for (int c = 0; ok && c < kFfChunks; ++c) {
+          ok = ff1(g0 + c);
+          if (ok && c == kFfChunks - 1) mma_commit(h_empty);  // h is free once this tile's FF1 completes
+          if (ok && c > 0) ok = ff2(g0 + c - 1, c - 1, i);
+        }
+        if (ok) ok = ff2(g0 + kFfChunks - 1, kFfChunks - 1, i);
+        if (ok) mma_commit(a2_full);
+      }
+    }
+  } else if (warp < kEpiWarps) {
+    // ---------------- epilogue warps ----------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kFfRegsEpi));
+    EpiCtx x;
+    x.lane = lane;
+    x.q = warp & 3;  // TMEM lane quadrant this warp may access
+    x.part = warp >> 2;
+    x.c0 = x.part * kPartCols;
+    x.row = x.q * 32 + lane;
+    uint32_t* staging = reinterpret_cast<uint32_t*>(smem + kFfOffG);
+    x.quad = staging + x.q * kParts * kStageWords;
+    x.st.base = x.quad + x.part * kStageWords;
+    x.st.lane = lane;
+    x.st.phase = 0;
+    x.st.last_f32 = false;
+    x.bar_id = 1 + x.q;
+    float* consts = reinterpret_cast<float*>(smem + kFfOffConst);
+    x.consts = consts;
+    x.id = x.part * 4 + x.q;
+    epi.load_consts(consts, warp * 32 + lane, kEpiWarps * 32);
+    copy_consts(consts + kFfB1, b1, 1024, warp * 32 + lane, kEpiWarps * 32);
+    asm volatile("bar.sync 5, %0;" ::"n"(kEpiWarps * 32) : "memory");
+    const uint32_t lane_off = static_cast<uint32_t>(x.q * 32) << 16;
+    // this thread's row in G tile 2*part (+1 for the second 64 columns)
+    uint8_t* grow = smem + kFfOffG + (2 * x.part) * kFfTileBytes + x.row * 128;
+    int i = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++i) {
+      const TileDesc t = epi.tile(tile);
+      // The row epilogue reads this tile's fp32 residual (128 rows x 1 KB)
+      // after the four GELU chunks: start bringing it into L2 now, four
+      // 128-byte lines per thread, so that those reads do not wait for HBM.
+      if (epi.resid && (warp * 32 + lane) / 2 < t.rows) {
+        const char* rp = reinterpret_cast<const char*>(epi.resid + static_cast<size_t>(t.row0) * 256) +
+                         (warp * 32 + lane) * 512;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) prefetch_l2(rp + k * 128);
+      }
+      const int g0 = i * kFfChunks;
+      for (int c = 0; ok && c < kFfChunks; ++c) {
+        const int g = g0 + c;
+        if (!(ok = mbar_wait(a1_full, g & 1, abort_flag, status))) break;
+        tc_fence_after();
+        uint32_t v[4][32];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tmem_ld32(tmem + lane_off + x.c0 + 32 * b, v[b]);
+#pragma unroll
+        for (int b = 0; b < 4; ++b) tmem_ld_wait(v[b]);
+        // the chunk is in registers: FF1 of the next chunk may overwrite acc1
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a1_empty);
+        const float* bias = consts + kFfB1 + c * kFfChunk + x.c0;
+        uint32_t w[4][16];
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+#pragma unroll
+          for (int j4 = 0; j4 < 8; ++j4) {
+            const float4 bb = lds4(bias + 32 * b + 4 * j4);
+            const float2 g0v = gelu_as2(
+                __fadd2_rn(f2(__uint_as_float(v[b][4 * j4]), __uint_as_float(v[b][4 * j4 + 1])), f2(bb.x, bb.y)));
+            const float2 g1v = gelu_as2(
+                __fadd2_rn(f2(__uint_as_float(v[b][4 * j4 + 2]), __uint_as_float(v[b][4 * j4 + 3])), f2(bb.z, bb.w)));
+            w[b][2 * j4] = pack_f16x2(g0v.x, g0v.y);
+            w[b][2 * j4 + 1] = pack_f16x2(g1v.x, g1v.y);
+          }
+        }
+        // G may be rewritten once FF2 of the previous chunk has read it
+        if (!(ok = mbar_wait(g_empty, (g & 1) ^ 1u, abort_flag, status))) break;
+        // 16-byte vector j of a 128-byte G row sits at j ^ (row & 7)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          uint8_t* dst = grow + (b >> 1) * kFfTileBytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<uint4*>(dst + ((((b & 1) * 4 + k) ^ (x.row & 7)) << 4)) =
+                make_uint4(w[b][4 * k], w[b][4 * k + 1], w[b][4 * k + 2], w[b][4 * k + 3]);
+        }
+        // the tensor core reads G through the async proxy
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(g_full);
+      }
+      if (!ok) break;
+      if (!(ok = mbar_wait(a2_full, i & 1, abort_flag, status))) break;
+      tc_fence_after();
+      x.tm = tmem + lane_off + kFfChunk;
+      x.next_tile = tile + static_cast<int>(gridDim.x) < n_tiles ? tile + static_cast<int>(gridDim.x) : -1;
+      epi.run(t, x);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(a2_empty);
+      // G held the staging buffers: the next tile's GELU rewrites it only
+      // after every warp's stores have read their blocks
+      x.st.drain();
+      if (lane == 0) mbar_arrive(stage_free);
+      ok = mbar_wait(stage_free, i & 1, abort_flag, status);
+    }
+    if (lane == 0) tma_store_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kFfWarpMma) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 static int num_sms() {
@@ -1011,6 +1331,44 @@ cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2,
   ep.resid = resid;
   ep.np = to_params(next);
   return launch_gemm(ta, tb, ep, dense_tiles(M, 256), status, st);
+}
+
+cudaError_t gemm_ff_fused(const __half* h16, const __half* w1, const float* b1, const __half* w2, const float* b2,
+                          const float* resid, float* x, int M, const RowNorm& next, int* status, cudaStream_t st) {
+  static unsigned long long configured = 0;
+  cudaError_t e = once_per_device(configured, [] {
+    cudaError_t r = cudaFuncSetAttribute(ff_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFfSmem);
+    if (r != cudaSuccess) return r;
+    // setmaxnreg.inc waits until the block's launch registers cover the split;
+    // refuse to launch a build whose register count would not
+    cudaFuncAttributes fa;
+    r = cudaFuncGetAttributes(&fa, ff_fused_kernel);
+    if (r != cudaSuccess) return r;
+    if (fa.numRegs * kFfThreads < kEpiWarps * 32 * kFfRegsEpi + (kFfThreads - kEpiWarps * 32) * kFfRegsOther)
+      return cudaErrorInvalidConfiguration;
+    return cudaSuccess;
+  });
+  if (e != cudaSuccess) return e;
+  CUtensorMap th, tw1, tw2;
+  EpiRow256 ep;
+  e = make_map_2d(&th, h16, 256, M, 256 * 2, kBK, kBM);
+  if (e == cudaSuccess) e = make_map_2d(&tw1, w1, 256, 1024, 256 * 2, kBK, kFfChunk);
+  if (e == cudaSuccess) e = make_map_2d(&tw2, w2, 1024, 256, 1024 * 2, kBK, kFfChunk);
+  if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, x, 256, M);
+  if (e == cudaSuccess && next.h16) e = out_map16(&ep.maps.h16_map, next.h16, 256, M);
+  if (e != cudaSuccess) return e;
+  ep.M = M;
+  ep.n_tiles = 1;
+  ep.kblocks = 0;  // unused: the fused kernel walks its own K loops
+  ep.ntd = make_fastdiv(1, dense_tiles(M, 256));
+  ep.bias = b2;
+  ep.resid = resid;
+  ep.np = to_params(next);
+  const int tiles = dense_tiles(M, 256);
+  if (tiles <= 0) return cudaSuccess;
+  const int grid = tiles < num_sms() ? tiles : num_sms();
+  ff_fused_kernel<<<grid, kFfThreads, kFfSmem, st>>>(th, tw1, tw2, ep, b1, tiles, status);
+  return cudaGetLastError();
 }
 
 cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, int wband_cols, const float* bias,

@@ -62,6 +62,9 @@ cudaError_t gemm_ff1_gelu(const __half* h16, const __half* w1, const float* b1, 
                           cudaStream_t st);
 cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2, const float* resid, float* x, int M,
                            const RowNorm& next, int* status, cudaStream_t st);
+// FF1 -> GELU -> FF2 + residual in one kernel, without the [M][1024] intermediate
+cudaError_t gemm_ff_fused(const __half* h16, const __half* w1, const float* b1, const __half* w2, const float* b2,
+                          const float* resid, float* x, int M, const RowNorm& next, int* status, cudaStream_t st);
 cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, int wband_cols, const float* bias,
                            float* x, int T, int nb, const TileDesc* tiles, int n_tiles, const RowNorm& first,
                            int* status, cudaStream_t st);

@@ -86,6 +86,7 @@ def lib() -> C.CDLL:
         "lbrr_op_outproj_norm": ([vp, vp, vp, vp, vp, vp, vp, i64, vp], C.c_int),
         "lbrr_op_ff1_gelu": ([vp, vp, vp, vp, i64, vp], C.c_int),
         "lbrr_op_ff2_resid": ([vp, vp, vp, vp, vp, i64, vp], C.c_int),
+        "lbrr_op_feed_forward": ([vp, vp, vp, vp, vp, vp, vp, i64, vp], C.c_int),
         "lbrr_op_sync": ([vp], C.c_int),
         "lbrr_op_feed_forward_noalloc": ([vp, vp, vp, vp, vp, vp, vp, i64, vp], C.c_int),
         "lbrr_f32_to_f16_bits": ([C.c_float], C.c_uint16),
@@ -104,7 +105,7 @@ HEADER_SYMBOLS = [
     "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
     "lbrr_engine_sync", "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
     "lbrr_op_qkv_rope", "lbrr_op_attention", "lbrr_op_outproj_norm", "lbrr_op_ff1_gelu", "lbrr_op_ff2_resid",
-    "lbrr_op_sync", "lbrr_op_feed_forward_noalloc",
+    "lbrr_op_feed_forward", "lbrr_op_sync", "lbrr_op_feed_forward_noalloc",
 ]
 
 
@@ -281,6 +282,12 @@ def ff1_gelu(h16, w16, b1, ff1, stream=None):
 def ff2_resid(ff1, w16, b2, resid, x, stream=None):
     check(lib().lbrr_op_ff2_resid(_ptr(ff1), _ptr(w16), _ptr(b2), _ptr(resid), _ptr(x), ff1.shape[0],
                                   _stream(stream)))
+
+
+def feed_forward(h16, w1, b1, w2, b2, resid, x, stream=None):
+    """FF1 + GELU -> FF2 + residual in one kernel (no [rows][1024] intermediate)."""
+    check(lib().lbrr_op_feed_forward(_ptr(h16), _ptr(w1), _ptr(b1), _ptr(w2), _ptr(b2), _ptr(resid), _ptr(x),
+                                     h16.shape[0], _stream(stream)))
 
 
 def feed_forward_noalloc(h16, w1, b1, w2, b2, resid, x, stream=None):

@@ -147,6 +147,29 @@ def test_ff2_resid(lb, M):
     assert rel_err(x.cpu(), f @ w.T + b + r) < 1e-5
 
 
+@pytest.mark.parametrize("M", [1, 37, 129, 2294, 16058, 71362])
+def test_feed_forward_fused(lb, M):
+    """The fused FF kernel gives the two-kernel path (FF1 + GELU into an fp16
+    buffer, then FF2 + bias + residual) bit for bit: same fp16 GELU values,
+    same K order of the FF2 accumulation; and both match the fp32 model."""
+    h = cuda(f16(randn((M, 256), 60, 1.0)), torch.float16)
+    w1 = cuda(f16(randn((1024, 256), 61, 0.05)), torch.float16)
+    b1 = cuda(randn((1024,), 62, 0.05))
+    w2 = cuda(f16(randn((256, 1024), 63, 0.02)), torch.float16)
+    b2 = cuda(randn((256,), 64, 0.02))
+    r = cuda(randn((M, 256), 65, 1.0))
+    ff1 = torch.empty(M, 1024, dtype=torch.float16, device="cuda")
+    ref = torch.empty(M, 256, device="cuda")
+    lb.ff1_gelu(h, w1, b1, ff1)
+    lb.ff2_resid(ff1, w2, b2, r, ref)
+    got = torch.full((M, 256), float("nan"), device="cuda")
+    lb.feed_forward(h, w1, b1, w2, b2, r, got)
+    lb.op_sync()
+    assert torch.equal(got, ref)
+    model = f16(R.gelu_as(h.float().cpu() @ w1.float().cpu().T + b1.cpu())) @ w2.float().cpu().T + b2.cpu() + r.cpu()
+    assert rel_err(got.cpu(), model) < 1e-4
+
+
 def test_invalid_arguments_are_rejected(lb):
     with pytest.raises(lb.LbrrError) as ei:
         lb.check(lb.lib().lbrr_op_attention(None, None, None, 10, 62, 0, None))
