@@ -159,7 +159,8 @@ def time_dominant_kernel(torch, lbrr, T=1151, iters=10):
 
 
 def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
-    """Per-GEMM tensor throughput at M = 62*T (QKV, out-proj, FF1, FF2)."""
+    """Per-kernel tensor throughput at M = 62*T of the trunk GEMMs the forward
+    runs: QKV, out-projection and the fused feed-forward (FF1 -> GELU -> FF2)."""
     M = T * 62
     g = torch.Generator(device="cuda").manual_seed(1)
     h = torch.randn(M, 256, device="cuda", generator=g).half()
@@ -177,14 +178,12 @@ def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
     h2 = torch.empty(M, 256, device="cuda", dtype=torch.float16)
     w1 = (torch.randn(1024, 256, device="cuda", generator=g) * 0.02).half()
     b1 = torch.zeros(1024, device="cuda")
-    ff1 = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
     w2 = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
     xo = torch.empty(M, 256, device="cuda")
     cases = {
         "qkv": (lambda s: lbrr.qkv_rope(h, w_qkv, b16, cos, sin, qkv, T, 62, 0, stream=s), 2 * M * 1536 * 256),
         "out_proj": (lambda s: lbrr.outproj_norm(sc, wo, bo, x, gam, ao, h2, stream=s), 2 * M * 256 * 512),
-        "ff1": (lambda s: lbrr.ff1_gelu(h, w1, b1, ff1, stream=s), 2 * M * 1024 * 256),
-        "ff2": (lambda s: lbrr.ff2_resid(ff1, w2, bo, x, xo, stream=s), 2 * M * 256 * 1024),
+        "feed_forward": (lambda s: lbrr.feed_forward(h, w1, b1, w2, bo, x, xo, stream=s), 2 * 2 * M * 1024 * 256),
     }
     res = {}
     s = torch.cuda.Stream()
