@@ -303,7 +303,7 @@ __device__ __forceinline__ float tanh_fast(float x) {
 // and rounded again -- the rounding points of cuBLASLt f16-out QKV followed by
 // rope_q16_inplace / rope_k16 (src/main.rs:6157-6187, :3684-3754).
 struct EpiQKV : DenseTiles {
-  CUtensorMap out_map;  // qkv [M][1536] fp16, box 32 x 32, 64-byte swizzle
+  CUtensorMap out_map;  // qkv [M][1536] fp16, box 64 x 32, 128-byte swizzle
   const float* bias16;  // [1536], values already rounded to fp16
   const float* cos;     // [P][32]
   const float* sin;
@@ -368,11 +368,15 @@ struct EpiQKV : DenseTiles {
       }
       if (x.next_tile >= 0) prefetch(tile(x.next_tile), x);
     }
+    // Two 32-column blocks are staged together and leave as one 32 x 64 fp16
+    // store: 128-byte rows, whole L2 lines, half as many stores as 32 x 32.
+    uint32_t wp[32];
     for_each_block(x, [&](uint32_t(&v)[32], int c) {
       const int col = t.aux + c;
       const bool rot = col < 1024;
       const int pair0 = (col & 63) >> 1;
-      uint32_t w[16];
+      const bool odd = ((c - x.c0) >> 5) & 1;  // block index within the warp's columns, known at compile time
+      uint32_t* w = wp + (odd ? 16 : 0);
 #pragma unroll
       for (int j4 = 0; j4 < 4; ++j4) {
         const float4 b0 = lds4(x.consts + col + 8 * j4), b1 = lds4(x.consts + col + 8 * j4 + 4);
@@ -405,9 +409,11 @@ struct EpiQKV : DenseTiles {
           }
         }
       }
-      uint32_t* buf = x.st.f16_buf();
-      stage_row<16>(buf, w, x.lane);
-      store_2d(&out_map, buf, col, t.row0 + x.q * 32, x.lane);
+      if (odd) {
+        uint32_t* buf = x.st.f32_buf();  // the whole 4 KB buffer
+        stage_row<32>(buf, wp, x.lane);
+        store_2d(&out_map, buf, col - 32, t.row0 + x.q * 32, x.lane);
+      }
     });
   }
 };
@@ -460,7 +466,7 @@ struct RowNormParams {
 
 struct Row256Maps {
   CUtensorMap out_map;  // fp32 rows, box 32 x 32 (2-D) or 32 x 1 x 32 (3-D), 128-byte swizzle
-  CUtensorMap h16_map;  // fp16 rows (norm 1, 2), box 32 x 32 (x 1), 64-byte swizzle
+  CUtensorMap h16_map;  // fp16 rows (norm 1, 2), box 64 x 32 (x 1), 128-byte swizzle
 };
 
 // Constants of the dense row epilogue in shared memory (EpiRow256::load_consts).
@@ -558,42 +564,52 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
   quad_sync(x.bar_id);
   const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
   float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  // fp16 rows leave 64 columns at a time (32 x 64 blocks, 128-byte rows: whole
+  // L2 lines); the band-major final norm scatters 32-column blocks by hand
 #pragma unroll 1
-  for (int c = c0; c < c0 + kPartCols; c += 32) {
-    uint32_t v[32];
-    tmem_ld32(x.tm + c, v);
-    tmem_ld_wait(v);
-    uint32_t w[16];
+  for (int c2 = c0; c2 < c0 + kPartCols; c2 += 64) {
+    uint32_t wp[32];
 #pragma unroll
-    for (int j4 = 0; j4 < 8; ++j4) {
-      const float4 gm = ld4(gamma + c + 4 * j4);
-      const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
-      float h[4];
+    for (int hb = 0; hb < 2; ++hb) {
+      const int c = c2 + 32 * hb;
+      uint32_t v[32];
+      tmem_ld32(x.tm + c, v);
+      tmem_ld_wait(v);
+      uint32_t* w = wp + 16 * hb;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const float vv = __uint_as_float(v[4 * j4 + k]);
-        h[k] = np.norm == 2 ? __fmul_rn(vv, __fmul_rn(scale, gg[k])) : __fmul_rn(__fmul_rn(vv, scale), gg[k]);
-      }
-      if (np.norm == 2) {
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 gm = ld4(gamma + c + 4 * j4);
+        const float gg[4] = {gm.x, gm.y, gm.z, gm.w};
+        float h[4];
 #pragma unroll
-        for (int gi = 0; gi < 8; ++gi) {
-          const float4 wg = ld4(gate_w + gi * 256 + c + 4 * j4);
-          g[gi] += h[0] * wg.x + h[1] * wg.y + h[2] * wg.z + h[3] * wg.w;
+        for (int k = 0; k < 4; ++k) {
+          const float vv = __uint_as_float(v[4 * j4 + k]);
+          h[k] = np.norm == 2 ? __fmul_rn(vv, __fmul_rn(scale, gg[k])) : __fmul_rn(__fmul_rn(vv, scale), gg[k]);
         }
+        if (np.norm == 2) {
+#pragma unroll
+          for (int gi = 0; gi < 8; ++gi) {
+            const float4 wg = ld4(gate_w + gi * 256 + c + 4 * j4);
+            g[gi] += h[0] * wg.x + h[1] * wg.y + h[2] * wg.z + h[3] * wg.w;
+          }
+        }
+        w[2 * j4] = pack_f16x2(h[0], h[1]);
+        w[2 * j4 + 1] = pack_f16x2(h[2], h[3]);
       }
-      w[2 * j4] = pack_f16x2(h[0], h[1]);
-      w[2 * j4 + 1] = pack_f16x2(h[2], h[3]);
+      if (np.norm == 3) {
+        uint32_t* buf = x.st.f16_buf();
+        stage_row<16>(buf, w, x.lane);
+        store_rows16_manual(buf, x.lane, [&](int r) -> char* {
+          if (rb + r >= t.rows) return nullptr;
+          const int tok = row_of(rb + r), tt = tok / np.nb, bb = tok % np.nb;
+          return reinterpret_cast<char*>(np.xb16 + (static_cast<size_t>(bb) * np.T + tt) * 256 + c);
+        });
+      }
     }
-    uint32_t* buf = x.st.f16_buf();
-    stage_row<16>(buf, w, x.lane);
-    if (np.norm == 3) {
-      store_rows16_manual(buf, x.lane, [&](int r) -> char* {
-        if (rb + r >= t.rows) return nullptr;
-        const int tok = row_of(rb + r), tt = tok / np.nb, bb = tok % np.nb;
-        return reinterpret_cast<char*>(np.xb16 + (static_cast<size_t>(bb) * np.T + tt) * 256 + c);
-      });
-    } else {
-      store_out(&maps.h16_map, buf, c);
+    if (np.norm != 3) {
+      uint32_t* buf = x.st.f32_buf();  // the whole 4 KB buffer
+      stage_row<32>(buf, wp, x.lane);
+      store_out(&maps.h16_map, buf, c2);
     }
   }
   if (np.norm == 2) {
@@ -657,28 +673,34 @@ struct EpiBand : TableTiles {
 // Mask estimator layer 1: hidden = f16(tanh(acc + b1)) (mask_gemm1_f16,
 // src/main.rs:4816-4842).  Tile aux = group*4 + n-tile, group = stem*nb + band.
 struct EpiTanh : TableTiles {
-  CUtensorMap out_map;  // hidden [groups][T][1024] fp16, box 32 x 32 x 1, 64-byte swizzle
+  CUtensorMap out_map;  // hidden [groups][T][1024] fp16, box 64 x 32 x 1, 128-byte swizzle
   const float* bias;    // [groups][1024]
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int group = t.aux >> 2, n0 = (t.aux & 3) * kBN;
+    // 64 columns per store: 32 x 64 fp16 blocks, 128-byte rows (whole L2 lines)
 #pragma unroll 1
-    for (int c = x.c0; c < x.c0 + kPartCols; c += 32) {
-      uint32_t v[32];
-      tmem_ld32(x.tm + c, v);
-      tmem_ld_wait(v);
-      const float* bb = bias + static_cast<size_t>(group) * 1024 + n0 + c;
-      uint32_t w[16];
+    for (int c2 = x.c0; c2 < x.c0 + kPartCols; c2 += 64) {
+      uint32_t wp[32];
 #pragma unroll
-      for (int j4 = 0; j4 < 8; ++j4) {
-        const float4 b = ldg4(bb + 4 * j4);
-        w[2 * j4] =
-            pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4]) + b.x), tanh_fast(__uint_as_float(v[4 * j4 + 1]) + b.y));
-        w[2 * j4 + 1] =
-            pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4 + 2]) + b.z), tanh_fast(__uint_as_float(v[4 * j4 + 3]) + b.w));
+      for (int hb = 0; hb < 2; ++hb) {
+        const int c = c2 + 32 * hb;
+        uint32_t v[32];
+        tmem_ld32(x.tm + c, v);
+        tmem_ld_wait(v);
+        const float* bb = bias + static_cast<size_t>(group) * 1024 + n0 + c;
+        uint32_t* w = wp + 16 * hb;
+#pragma unroll
+        for (int j4 = 0; j4 < 8; ++j4) {
+          const float4 b = ldg4(bb + 4 * j4);
+          w[2 * j4] =
+              pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4]) + b.x), tanh_fast(__uint_as_float(v[4 * j4 + 1]) + b.y));
+          w[2 * j4 + 1] = pack_f16x2(tanh_fast(__uint_as_float(v[4 * j4 + 2]) + b.z),
+                                     tanh_fast(__uint_as_float(v[4 * j4 + 3]) + b.w));
+        }
       }
-      uint32_t* buf = x.st.f16_buf();
-      stage_row<16>(buf, w, x.lane);
-      store_3d(&out_map, buf, n0 + c, t.row0 + x.q * 32, group, x.lane);
+      uint32_t* buf = x.st.f32_buf();  // the whole 4 KB buffer
+      stage_row<32>(buf, wp, x.lane);
+      store_3d(&out_map, buf, n0 + c2, t.row0 + x.q * 32, group, x.lane);
     }
   }
 };
@@ -1236,6 +1258,11 @@ static cudaError_t out_map16(CUtensorMap* m, const void* base, int cols, uint64_
   return make_map_2d(m, base, cols, rows, static_cast<uint64_t>(cols) * 2, 32, 32, MapElem::F16,
                      CU_TENSOR_MAP_SWIZZLE_64B);
 }
+// fp16 [rows][cols] output map for 32 x 64 blocks (128-byte rows, 128-byte swizzle)
+static cudaError_t out_map16w(CUtensorMap* m, const void* base, int cols, uint64_t rows) {
+  return make_map_2d(m, base, cols, rows, static_cast<uint64_t>(cols) * 2, 64, 32, MapElem::F16,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
 // fp32 [rows][cols] output map for 32 x 32 blocks (128-byte rows, 128-byte swizzle)
 static cudaError_t out_map32(CUtensorMap* m, const void* base, int cols, uint64_t rows) {
   return make_map_2d(m, base, cols, rows, static_cast<uint64_t>(cols) * 4, 32, 32, MapElem::F32,
@@ -1261,7 +1288,8 @@ cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, co
   EpiQKV ep;
   cudaError_t e = make_map_2d(&ta, h16, 256, M, 256 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w, 256, 1536, 256 * 2, kBK, kBN);
-  if (e == cudaSuccess) e = out_map16(&ep.out_map, qkv, 1536, M);
+  if (e == cudaSuccess)
+    e = make_map_2d(&ep.out_map, qkv, 1536, M, 1536 * 2, 64, 32, MapElem::F16, CU_TENSOR_MAP_SWIZZLE_128B);
   if (e != cudaSuccess) return e;
   ep.M = M;
   ep.n_tiles = 1536 / kBN;
@@ -1283,7 +1311,7 @@ cudaError_t gemm_outproj_norm(const __half* scaled16, const __half* w, const flo
   cudaError_t e = make_map_2d(&ta, scaled16, 512, M, 512 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w, 512, 256, 512 * 2, kBK, kBN);
   if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, out, 256, M);
-  if (e == cudaSuccess) e = out_map16(&ep.maps.h16_map, h16, 256, M);
+  if (e == cudaSuccess) e = out_map16w(&ep.maps.h16_map, h16, 256, M);
   if (e != cudaSuccess) return e;
   ep.M = M;
   ep.n_tiles = 1;
@@ -1321,7 +1349,7 @@ cudaError_t gemm_ff2_resid(const __half* ff1, const __half* w2, const float* b2,
   cudaError_t e = make_map_2d(&ta, ff1, 1024, M, 1024 * 2, kBK, kBM);
   if (e == cudaSuccess) e = make_map_2d(&tb, w2, 1024, 256, 1024 * 2, kBK, kBN);
   if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, x, 256, M);
-  if (e == cudaSuccess && next.h16) e = out_map16(&ep.maps.h16_map, next.h16, 256, M);
+  if (e == cudaSuccess && next.h16) e = out_map16w(&ep.maps.h16_map, next.h16, 256, M);
   if (e != cudaSuccess) return e;
   ep.M = M;
   ep.n_tiles = 1;
@@ -1355,7 +1383,7 @@ cudaError_t gemm_ff_fused(const __half* h16, const __half* w1, const float* b1, 
   if (e == cudaSuccess) e = make_map_2d(&tw1, w1, 256, 1024, 256 * 2, kBK, kFfChunk);
   if (e == cudaSuccess) e = make_map_2d(&tw2, w2, 1024, 256, 1024 * 2, kBK, kFfChunk);
   if (e == cudaSuccess) e = out_map32(&ep.maps.out_map, x, 256, M);
-  if (e == cudaSuccess && next.h16) e = out_map16(&ep.maps.h16_map, next.h16, 256, M);
+  if (e == cudaSuccess && next.h16) e = out_map16w(&ep.maps.h16_map, next.h16, 256, M);
   if (e != cudaSuccess) return e;
   ep.M = M;
   ep.n_tiles = 1;
@@ -1385,8 +1413,8 @@ cudaError_t gemm_bandsplit(const __half* xn, int xn_cols, const __half* wband, i
     e = make_map_3d(&ep.maps.out_map, x, 256, nb, T, 256 * 4, static_cast<uint64_t>(nb) * 256 * 4, 32, 1, 32,
                     MapElem::F32, CU_TENSOR_MAP_SWIZZLE_128B);
   if (e == cudaSuccess && first.h16)
-    e = make_map_3d(&ep.maps.h16_map, first.h16, 256, nb, T, 256 * 2, static_cast<uint64_t>(nb) * 256 * 2, 32, 1,
-                    32, MapElem::F16, CU_TENSOR_MAP_SWIZZLE_64B);
+    e = make_map_3d(&ep.maps.h16_map, first.h16, 256, nb, T, 256 * 2, static_cast<uint64_t>(nb) * 256 * 2, 64, 1,
+                    32, MapElem::F16, CU_TENSOR_MAP_SWIZZLE_128B);
   if (e != cudaSuccess) return e;
   ep.table = tiles;
   ep.bias = bias;
@@ -1403,8 +1431,8 @@ cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __
   if (e == cudaSuccess) e = make_map_2d(&tb, w1, 256, static_cast<uint64_t>(groups) * 1024, 256 * 2, kBK, kBN);
   // hidden viewed as [groups][T][1024] so a tile's rows never spill into the next group
   if (e == cudaSuccess)
-    e = make_map_3d(&ep.out_map, hidden, 1024, T, groups, 1024 * 2, static_cast<uint64_t>(T) * 1024 * 2, 32, 32, 1,
-                    MapElem::F16, CU_TENSOR_MAP_SWIZZLE_64B);
+    e = make_map_3d(&ep.out_map, hidden, 1024, T, groups, 1024 * 2, static_cast<uint64_t>(T) * 1024 * 2, 64, 32, 1,
+                    MapElem::F16, CU_TENSOR_MAP_SWIZZLE_128B);
   if (e != cudaSuccess) return e;
   ep.table = tiles;
   ep.bias = b1;
