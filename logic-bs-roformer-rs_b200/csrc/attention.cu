@@ -337,8 +337,11 @@ __global__ void __launch_bounds__(kT1Threads, 2)
 // ---------------------------------------------------------------------------
 // Frequency axis: persistent CTAs, one (frame pair, head) item at a time
 // ---------------------------------------------------------------------------
-// Each item is two sequences of nb = 62 band tokens (frames 2p and 2p+1) packed
-// into one 128-row tile with a block-diagonal mask, one key tile.  An item is
+// Each item is two sequences of nb <= 64 band tokens (frames 2p and 2p+1)
+// packed into one 128-row tile, frame 2p at rows 0.., frame 2p+1 at rows
+// 64.. (two TMA boxes per operand; the padding rows are zeroed once), with a
+// block-diagonal mask: every warp's 32 rows belong to one sequence and see
+// exactly two 32-key chunks of S, read once into registers.  An item is
 // small (48 KB of Q/K/V), so its load latency, not its math, set the time of a
 // one-item CTA; here each CTA (two per SM) walks items with a stride of the
 // grid and a 2-stage TMA ring: item k+1's Q/K/V arrive while item k runs.
@@ -388,6 +391,15 @@ __global__ void __launch_bounds__(kFThreads, 2)
     tmem_alloc(tmem_slot, kAttnTmemCols);
     tmem_relinquish();
   }
+  // Rows nb..63 and 64+nb..127 of every Q/K/V tile are never loaded: zero
+  // them once (P is 0 for those keys, and 0 times a stale NaN would not be).
+  for (int i = threadIdx.x; i < kFStages * 3 * 2 * 16; i += kFThreads) {
+    const int tile = i >> 5, half = (i >> 4) & 1, v = i & 15;  // 16 B pieces of a 256-byte span
+    uint8_t* t0 = smem + tile * kTile + half * 64 * 128;
+    for (int off = nb * 128 + v * 16; off < 64 * 128; off += 256)
+      *reinterpret_cast<uint4*>(t0 + off) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -402,10 +414,10 @@ __global__ void __launch_bounds__(kFThreads, 2)
         if (!mbar_wait(&empty[st], ((k >> 1) & 1) ^ 1u, abort_flag, a.status)) break;
         const int head = it & 7, row0 = (it >> 3) * 2 * nb;
         uint8_t* s = smem + st * kFStage;
-        mbar_arrive_expect_tx(&full[st], 3 * kTile);
-        tma_load_2d(s, &tm, &full[st], head * 64, row0);
-        tma_load_2d(s + kTile, &tm, &full[st], 512 + head * 64, row0);
-        tma_load_2d(s + 2 * kTile, &tm, &full[st], 1024 + head * 64, row0);
+        mbar_arrive_expect_tx(&full[st], 3 * 2 * nb * 128);
+        for (int h = 0; h < 2; ++h)
+          for (int m = 0; m < 3; ++m)
+            tma_load_2d(s + m * kTile + h * 64 * 128, &tm, &full[st], m * 512 + head * 64, row0 + h * nb);
       }
     }
   } else if (warp == 1) {
@@ -446,59 +458,54 @@ __global__ void __launch_bounds__(kFThreads, 2)
     const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
     const uint32_t tS = tmem + lane_off + kColS, tO = tmem + lane_off + kColO, tP = tmem + lane_off + kColP;
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
-    const int rseq = r / nb;                        // which of the two packed sequences
-    const int lo = rseq * nb, hi = lo + nb;         // this row's keys
+    const int rseq = r >> 6;                        // which of the two packed sequences (warp-uniform)
+    const int ri = r & 63;                          // token index within it
     bool ok = true;
     int k = 0;
     for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++k) {
       const int head = it & 7, t = (it >> 3) * 2 + rseq;
-      const bool valid = r < 2 * nb && t < T;
-      const int token = t * nb + (r - lo);
+      const bool valid = ri < nb && t < T;
+      const int token = t * nb + ri;
       // the gate is independent of the MMAs: fetch it before waiting
       const float gate = valid ? __ldg(a.gates + static_cast<size_t>(token) * 8 + head) : 0.f;
       ok = mbar_wait(s_full, k & 1, abort_flag, a.status);
       if (!ok) break;
       tc_fence_after();
-      // Two passes over S in 32-key chunks (S stays in TMEM until the next
-      // item): the row max, then the exponentials, each chunk's P stored as it
-      // is done.  A chunk none of the warp's rows has keys in is skipped; its
-      // P is written as zeros, since the PV MMA reads all 128 keys.
+      // the row's keys are S columns 64*rseq .. 64*rseq + nb - 1: two chunks
+      uint32_t v[2][32];
+      tmem_ld32(tS + rseq * 64, v[0]);
+      tmem_ld32(tS + rseq * 64 + 32, v[1]);
+      tmem_ld_wait(v[0]);
+      tmem_ld_wait(v[1]);
       float mx = -INFINITY;
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        if (!__any_sync(0xffffffffu, q4 * 32 < hi && q4 * 32 + 32 > lo)) continue;
-        uint32_t v[32];
-        tmem_ld32(tS + q4 * 32, v);
-        tmem_ld_wait(v);
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int c = 0; c < 32; ++c)
-          if (q4 * 32 + c >= lo && q4 * 32 + c < hi) mx = fmaxf(mx, __uint_as_float(v[c]));
-      }
+          if (h * 32 + c < nb) mx = fmaxf(mx, __uint_as_float(v[h][c]));
       const float msc = (mx == -INFINITY ? 0.f : mx) * sc;
       float2 sum2 = make_float2(0.f, 0.f);
+      uint32_t zero[16];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int c = 0; c < 16; ++c) zero[c] = 0u;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
         uint32_t w[16];
-        if (__any_sync(0xffffffffu, q4 * 32 < hi && q4 * 32 + 32 > lo)) {
-          uint32_t v[32];
-          tmem_ld32(tS + q4 * 32, v);
-          tmem_ld_wait(v);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int c0 = q4 * 32 + 2 * c;
-            const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(v[2 * c]), __uint_as_float(v[2 * c + 1])),
-                                         make_float2(sc, sc), make_float2(-msc, -msc));
-            float2 p = make_float2(ex2(a2.x), ex2(a2.y));
-            p.x = (c0 >= lo && c0 < hi) ? p.x : 0.f;
-            p.y = (c0 + 1 >= lo && c0 + 1 < hi) ? p.y : 0.f;
-            sum2 = __fadd2_rn(sum2, p);
-            w[c] = pack_f16x2(p.x, p.y);
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 16; ++c) w[c] = 0u;
+        for (int c = 0; c < 16; ++c) {
+          const int kk = h * 32 + 2 * c;
+          const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(v[h][2 * c]), __uint_as_float(v[h][2 * c + 1])),
+                                       make_float2(sc, sc), make_float2(-msc, -msc));
+          float2 p = make_float2(ex2(a2.x), ex2(a2.y));
+          p.x = kk < nb ? p.x : 0.f;
+          p.y = kk + 1 < nb ? p.y : 0.f;
+          sum2 = __fadd2_rn(sum2, p);
+          w[c] = pack_f16x2(p.x, p.y);
         }
-        tmem_st16(tP + q4 * 16, w);
+        // P columns hold key pairs: this sequence's keys at 32*rseq.., the
+        // other sequence's (masked) at 32*(1-rseq)..
+        tmem_st16(tP + rseq * 32 + h * 16, w);
+        tmem_st16(tP + (1 - rseq) * 32 + h * 16, zero);
       }
       const float l = sum2.x + sum2.y;
       tmem_st_wait();
@@ -560,7 +567,7 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   });
   if (ce != cudaSuccess) return ce;
   if (T <= 0) return cudaSuccess;
-  if (axis == 1 && 2 * nb > 128) return cudaErrorInvalidValue;  // two sequences per 128-row tile
+  if (axis == 1 && nb > 64) return cudaErrorInvalidValue;  // two sequences of <= 64 tokens per 128-row tile
   CUtensorMap tm;
   cudaError_t e;
   AttnArgs a;
@@ -578,7 +585,8 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     attn_time_kernel<<<dim3(a.nk, nb * 8), kT1Threads, kT1Smem, st>>>(tm, a);
     return cudaGetLastError();
   }
-  e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, 128);
+  // boxes of one frame's nb tokens
+  e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, nb);
   if (e != cudaSuccess) return e;
   a.nk = 1;
   // (frame pair, head) items over two persistent CTAs per SM

@@ -81,6 +81,22 @@ def test_attention(lb, T, axis):
     assert snr_db(got, ref) > 55.0, snr_db(got, ref)
 
 
+@pytest.mark.parametrize("T,nb", [(5, 40), (3, 64), (4, 1)])
+def test_attention_freq_band_counts(lb, T, nb):
+    """Frequency axis with band counts other than 62: each frame's nb tokens
+    sit at rows 0.. and 64.. of the packed tile, the padding rows zeroed."""
+    M = T * nb
+    qkv = f16(randn((M, 1536), 70 + nb, 1.0))
+    gates = randn((M, 8), 71, 1.0)
+    out = torch.empty(M, 512, dtype=torch.float16, device="cuda")
+    lb.attention(cuda(qkv, torch.float16), cuda(gates), out, T, nb, 1)
+    lb.op_sync()
+    ref = oracle_attention_gated(qkv, gates, T, nb, 1)
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    assert snr_db(got, ref) > 55.0, snr_db(got, ref)
+
+
 def test_attention_max_jump(lb):
     """Time axis: keys of the second and third key tiles score far above the
     first tile's, so the row max grows by more than 2^8 in exp2 units mid-row
