@@ -720,23 +720,46 @@ struct EpiMask : TableTiles {
   float2* out;          // [stems*2][T][1025]
   int T, n2tot;
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
-    const int r = t.row0 + x.row;
     const bool valid = x.row < t.rows;
+    const int rb = x.q * 32;                // this warp's first tile row
+    const int rows_valid = min(32, t.rows - rb);
+    const int r0 = t.row0 + rb;             // its first frame
     const int stem = t.aux >> 16, band = (t.aux >> 8) & 255, n0 = (t.aux & 255) * kBN;
     const int d_b = band_d[band], f0 = band_f0[band];
     const float* bb = bias2 + static_cast<size_t>(stem) * n2tot + band_o2[band] + n0;
     const int c_end = min(x.c0 + kPartCols, t.n);
+    // A 32-column block is 4 bins of 32 frames.  Spectrum values go through
+    // the warp's staging buffer ([2 channels][32 frames][4 bins] float2): read
+    // with four lanes per frame (32 contiguous bytes), masked by the frame's
+    // lane, written back the same way, instead of one 8-byte access per lane
+    // at a stride of a whole frame.
+    float2* sbuf = reinterpret_cast<float2*>(x.st.base);
+    const int lrow = x.lane >> 2, lbin = x.lane & 3;
 #pragma unroll 1
     for (int c = x.c0; c < c_end; c += 32) {
       uint32_t v[32];
       tmem_ld32(x.tm + c, v);
-      tmem_ld_wait(v);
-      if (!valid) continue;
+      // bins of this block with columns in the tile and inside the band (a prefix)
+      int nbins = 0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int lc = c + q * 8;        // column inside this tile
-        const int d0 = (n0 + lc) >> 1;  // first GLU index of this bin = fi*4
-        if (lc < t.n && d0 < d_b) {
+      for (int q = 0; q < 4; ++q) nbins += (c + q * 8 < t.n && ((n0 + c + q * 8) >> 1) < d_b) ? 1 : 0;
+      const int fb = f0 + ((n0 + c) >> 3);  // first bin
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int row = it * 8 + lrow;
+        if (row < rows_valid && lbin < nbins)
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch)
+            sbuf[(ch * 32 + row) * 4 + lbin] = spec[(static_cast<size_t>(ch) * T + r0 + row) * 1025 + fb + lbin];
+      }
+      tmem_ld_wait(v);
+      __syncwarp();
+      if (valid) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          if (q >= nbins) break;
+          const int lc = c + q * 8;  // column inside this tile
           float m[4];
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
@@ -744,22 +767,34 @@ struct EpiMask : TableTiles {
             const float g = __uint_as_float(v[q * 8 + 2 * k + 1]) + __ldg(bb + lc + 2 * k + 1);
             m[k] = __fdividef(a, 1.0f + __expf(-g));
           }
-          const int f = f0 + (d0 >> 2);
+          const int f = fb + q;
 #pragma unroll
           for (int ch = 0; ch < 2; ++ch) {
-            const float2 s = spec[(static_cast<size_t>(ch) * T + r) * 1025 + f];
+            float2& slot = sbuf[(ch * 32 + x.lane) * 4 + q];
+            const float2 sp = slot;
             const float mr = m[2 * ch], mi = m[2 * ch + 1];
             float2 o;
-            o.x = s.x * mr - s.y * mi;
+            o.x = sp.x * mr - sp.y * mi;
             // A real signal's DC and Nyquist bins are real: torch.istft drops
             // their imaginary parts, and cuFFT's C2R is only defined for such
             // Hermitian input, so the masked spectrum keeps them real.
-            o.y = (f == 0 || f == 1024) ? 0.f : s.x * mi + s.y * mr;
-            out[(static_cast<size_t>(stem * 2 + ch) * T + r) * 1025 + f] = o;
+            o.y = (f == 0 || f == 1024) ? 0.f : sp.x * mi + sp.y * mr;
+            slot = o;
           }
         }
       }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int row = it * 8 + lrow;
+        if (row < rows_valid && lbin < nbins)
+#pragma unroll
+          for (int ch = 0; ch < 2; ++ch)
+            out[(static_cast<size_t>(stem * 2 + ch) * T + r0 + row) * 1025 + fb + lbin] =
+                sbuf[(ch * 32 + row) * 4 + lbin];
+      }
     }
+    __syncwarp();
   }
 };
 
