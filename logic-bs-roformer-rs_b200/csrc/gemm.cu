@@ -341,7 +341,35 @@ struct EpiQKV : DenseTiles {
     const int row = x.lane >> 4, k4 = (x.lane & 15) * 4;
     if (row < span) x.pre = ldg4((k4 < 32 ? cos + k4 : sin + (k4 - 32)) + (p_lo + row) * 32);
   }
+  // V columns (n-tiles 4 and 5): bias only, no rotation and no RoPE rows
+  __device__ void run_v(const TileDesc& t, EpiCtx& x) const {
+    if (axis == 0 && x.next_tile >= 0) prefetch(tile(x.next_tile), x);
+    uint32_t wp[32];
+    for_each_block(x, [&](uint32_t(&v)[32], int c) {
+      const int col = t.aux + c;
+      const bool odd = ((c - x.c0) >> 5) & 1;  // block index within the warp's columns, known at compile time
+      uint32_t* w = wp + (odd ? 16 : 0);
+#pragma unroll
+      for (int j4 = 0; j4 < 8; ++j4) {
+        const float4 b = lds4(x.consts + col + 4 * j4);
+        const float2 e0 = __fadd2_rn(f2(__uint_as_float(v[4 * j4]), __uint_as_float(v[4 * j4 + 1])), f2(b.x, b.y));
+        const float2 e1 =
+            __fadd2_rn(f2(__uint_as_float(v[4 * j4 + 2]), __uint_as_float(v[4 * j4 + 3])), f2(b.z, b.w));
+        w[2 * j4] = pack_f16x2(e0.x, e0.y);
+        w[2 * j4 + 1] = pack_f16x2(e1.x, e1.y);
+      }
+      if (odd) {
+        uint32_t* buf = x.st.f32_buf();  // the whole 4 KB buffer
+        stage_row<32>(buf, wp, x.lane);
+        store_2d(&out_map, buf, col - 32, t.row0 + x.q * 32, x.lane);
+      }
+    });
+  }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
+    if (t.aux >= 1024) {
+      run_v(t, x);
+      return;
+    }
     const int r = t.row0 + x.row;
     const bool valid = x.row < t.rows;
     const int pq = nbd.div(r);
