@@ -211,11 +211,12 @@ __global__ void __launch_bounds__(kT1Threads, 2)
       if (!ok) break;
       tc_fence_after();
       const int hi = min(128, T - j * 128);  // valid keys of this tile: [0, hi)
-      uint32_t s[4][32];
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(tS + q4 * 32, s[q4]);
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld_wait(s[q4]);
+      uint32_t s_row[2][64];
+      tmem_ld64(tS, s_row[0]);
+      tmem_ld64(tS + 64, s_row[1]);
+      tmem_ld_wait64(s_row[0]);
+      tmem_ld_wait64(s_row[1]);
+      uint32_t(&s)[4][32] = *reinterpret_cast<uint32_t(*)[4][32]>(s_row);
       // S is in registers: the MMA warp may overwrite it with the next tile
       tc_fence_before();
       mbar_arrive(s_free);
@@ -292,8 +293,7 @@ __global__ void __launch_bounds__(kT1Threads, 2)
           tmem_st_wait();
         }
       }
-      tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(w));
-      tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(w + 32));
+      tmem_st64(tP, w);
       tmem_st_wait();
       l_run = l_run * corr + sum;
       m_run = m_next;
