@@ -10,7 +10,9 @@
 #include <condition_variable>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -147,6 +149,74 @@ struct StepWeights {
 
 constexpr int kHostSlices = 8;  // slices of the stem download in lbrr_forward_chunk_host
 
+// Threads kept by an engine for its host entry point: the copies between the
+// caller's (pageable) buffers and pinned memory run on kHostWorkers threads,
+// the calling thread being worker 0, without starting threads on every call.
+constexpr int kHostWorkers = 4;
+class HostPool {
+ public:
+  HostPool() {
+    for (int w = 1; w < kHostWorkers; ++w) th_.emplace_back([this, w] { loop(w); });
+  }
+  ~HostPool() {
+    {
+      std::lock_guard<std::mutex> l(m_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : th_) t.join();
+  }
+  // f(w) for w = 0 .. kHostWorkers-1 (0 on the calling thread); returns once all are done
+  void run(const std::function<void(int)>& f) {
+    {
+      std::lock_guard<std::mutex> l(m_);
+      job_ = &f;
+      pending_ = kHostWorkers - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    f(0);
+    std::unique_lock<std::mutex> l(m_);
+    done_.wait(l, [&] { return pending_ == 0; });
+    job_ = nullptr;
+  }
+
+ private:
+  void loop(int w) {
+    uint64_t seen = 0;
+    for (;;) {
+      const std::function<void(int)>* f = nullptr;
+      {
+        std::unique_lock<std::mutex> l(m_);
+        cv_.wait(l, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+        f = job_;
+      }
+      (*f)(w);
+      {
+        std::lock_guard<std::mutex> l(m_);
+        --pending_;
+      }
+      done_.notify_one();
+    }
+  }
+  std::vector<std::thread> th_;
+  std::mutex m_;
+  std::condition_variable cv_, done_;
+  const std::function<void(int)>* job_ = nullptr;
+  uint64_t gen_ = 0;
+  int pending_ = 0;
+  bool stop_ = false;
+};
+
+// Byte range [lo, hi) of worker w's share of n bytes (64-byte aligned cuts).
+static inline void host_share(size_t n, int w, size_t& lo, size_t& hi) {
+  const size_t part = (n / kHostWorkers + 63) / 64 * 64;
+  lo = std::min(n, part * static_cast<size_t>(w));
+  hi = std::min(n, lo + part);
+}
+
 struct lbrr_engine {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -205,8 +275,10 @@ struct lbrr_engine {
   int64_t graph_len = -1;
   cudaStream_t graph_stream = nullptr;
   int graph_seen = 0;
-  // lbrr_forward_chunk_host: one event per downloaded slice of the stems
+  // lbrr_forward_chunk_host: one event per downloaded slice of the stems, and
+  // the host threads that copy them (started by the first call)
   cudaEvent_t host_ev[kHostSlices] = {};
+  std::unique_ptr<HostPool> host_pool;
 };
 
 namespace {
@@ -440,6 +512,7 @@ extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
   if (e->graph) cudaGraphExecDestroy(e->graph);
   for (auto& ev : e->host_ev)
     if (ev) cudaEventDestroy(ev);
+  e->host_pool.reset();
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -928,28 +1001,11 @@ extern "C" int lbrr_engine_sync(lbrr_engine* e) {
   return check_status(e->status, e->stream);
 }
 
-// Host memcpy split over `n` threads (one stream of bytes per thread).
-static void parallel_memcpy(void* dst, const void* src, size_t bytes, int n) {
-  if (n <= 1 || bytes < (1u << 20)) {
-    std::memcpy(dst, src, bytes);
-    return;
-  }
-  std::vector<std::thread> th;
-  const size_t part = (bytes / n + 63) / 64 * 64;
-  for (int i = 1; i < n; ++i) {
-    const size_t o = part * i;
-    if (o >= bytes) break;
-    th.emplace_back([=] {
-      std::memcpy(static_cast<char*>(dst) + o, static_cast<const char*>(src) + o, std::min(part, bytes - o));
-    });
-  }
-  std::memcpy(dst, src, std::min(part, bytes));
-  for (auto& t : th) t.join();
-}
-
 // The stems leave the GPU in kHostSlices slices, each followed by an event;
-// host threads copy a slice from pinned memory into the caller's buffer as
-// soon as it has arrived, so the host copy overlaps the rest of the download.
+// the engine's host threads copy every slice, a quarter each, from pinned
+// memory into the caller's buffer as soon as it has arrived, so the host copy
+// overlaps the rest of the download and the last slice's copy is short.  The
+// input is staged into pinned memory by the same threads.
 extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t len, float* outh) {
   if (int rc = check_forward_args(e, xh, len, outh)) return rc;
   DeviceGuard g(e->device);
@@ -957,7 +1013,18 @@ extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t 
   const size_t out_b = static_cast<size_t>(len) * 2 * kStems * sizeof(float);
   for (auto& ev : e->host_ev)
     if (!ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
-  parallel_memcpy(e->pin_in, xh, in_b, 4);
+  const bool threaded = out_b >= (4u << 20);
+  if (threaded && !e->host_pool) e->host_pool = std::make_unique<HostPool>();
+  if (threaded) {
+    e->host_pool->run([&](int w) {
+      size_t lo, hi;
+      host_share(in_b, w, lo, hi);
+      if (hi > lo)
+        std::memcpy(reinterpret_cast<char*>(e->pin_in) + lo, reinterpret_cast<const char*>(xh) + lo, hi - lo);
+    });
+  } else {
+    std::memcpy(e->pin_in, xh, in_b);
+  }
   CK(cudaMemcpyAsync(e->dev_in, e->pin_in, in_b, cudaMemcpyHostToDevice, e->stream));
   if (int rc = lbrr_forward_chunk(e, e->dev_in, len, e->dev_out, e->stream)) return rc;
   const size_t slice = (out_b / kHostSlices + 255) / 256 * 256;
@@ -968,23 +1035,25 @@ extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t 
                        cudaMemcpyDeviceToHost, e->stream));
     CK(cudaEventRecord(e->host_ev[slices], e->stream));
   }
-  const int workers = out_b < (4u << 20) ? 1 : 4;
   std::atomic<int> copy_err{0};
   auto copy_slices = [&](int w) {
-    for (int i = w; i < slices; i += workers) {
+    for (int i = 0; i < slices; ++i) {
       if (cudaEventSynchronize(e->host_ev[i]) != cudaSuccess) {
         copy_err.store(1);
-        continue;
+        return;
       }
-      const size_t o = static_cast<size_t>(i) * slice;
-      std::memcpy(reinterpret_cast<char*>(outh) + o, reinterpret_cast<const char*>(e->pin_out) + o,
-                  std::min(slice, out_b - o));
+      const size_t o = static_cast<size_t>(i) * slice, n = std::min(slice, out_b - o);
+      size_t lo = 0, hi = n;
+      if (threaded) host_share(n, w, lo, hi);
+      if (hi > lo)
+        std::memcpy(reinterpret_cast<char*>(outh) + o + lo, reinterpret_cast<const char*>(e->pin_out) + o + lo,
+                    hi - lo);
     }
   };
-  std::vector<std::thread> th;
-  for (int w = 1; w < workers; ++w) th.emplace_back(copy_slices, w);
-  copy_slices(0);
-  for (auto& t : th) t.join();
+  if (threaded)
+    e->host_pool->run(copy_slices);
+  else
+    copy_slices(0);
   if (int rc = check_status(e->status, e->stream)) return rc;
   if (copy_err.load()) return fail(LBRR_ERR_CUDA, "stem download");
   return LBRR_OK;
