@@ -8,7 +8,6 @@ exercise only the host-side sharding logic; a rank that fails must make the
 others fail fast, not hang.
 """
 import datetime
-import socket
 
 import numpy as np
 import pytest
@@ -21,12 +20,6 @@ PLAN = dict(chunk=8192, step=7168, border=1024)
 LENGTH = 50000  # 7 chunks under PLAN
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
 def fake_model(xc: np.ndarray) -> np.ndarray:
     """[2][chunk] -> [6][2][chunk]: per-stem gains plus a ramp over the chunk
     position, so a misplaced chunk or a wrong fade shows up."""
@@ -36,10 +29,10 @@ def fake_model(xc: np.ndarray) -> np.ndarray:
     return (xc[None] * gains + pos * np.float32(0.01)).astype(np.float32)
 
 
-def _worker(rank, world, port, audio, out_path, fail_rank):
+def _worker(rank, world, init, audio, out_path, fail_rank):
     import torch
     import torch.distributed as dist
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=10))
     try:
         def forward(x, y):
@@ -56,9 +49,10 @@ def _worker(rank, world, port, audio, out_path, fail_rank):
 
 def _run(world, tmp_path, audio, fail_rank=-1):
     out = tmp_path / f"song_w{world}.npy"
-    port = _free_port()
+    # rendezvous through a file in the test's own directory: no port to race for
+    init = f"file://{tmp_path / f'store_w{world}_f{fail_rank}'}"
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, world, port, audio, str(out), fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, init, audio, str(out), fail_rank)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
