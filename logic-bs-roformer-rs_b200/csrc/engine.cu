@@ -257,11 +257,15 @@ struct lbrr_engine {
   float* dev_in = nullptr;
   float* dev_out = nullptr;
   // whole-song sharding (lbrr_separate_song): double-buffered pinned chunk
-  // input and region output, the finished region on the device, the overlap
-  // strip this engine produces, and the strips it receives (one per chunk)
+  // input and region output, the finished regions on the device (double-
+  // buffered: a region's download runs on song_copy while the next chunk is
+  // computed), the overlap strip this engine produces, and the strips it
+  // receives (one per chunk)
   float* song_pin_in[2] = {nullptr, nullptr};
   float* song_pin_out[2] = {nullptr, nullptr};
-  float* song_fin = nullptr;
+  float* song_fin[2] = {nullptr, nullptr};
+  cudaStream_t song_copy = nullptr;
+  cudaEvent_t song_ev_reg[2] = {nullptr, nullptr};
   float* song_strip_out = nullptr;
   float* song_strip_in = nullptr;
   size_t song_strip_in_bytes = 0;
@@ -505,8 +509,10 @@ extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
     if (e->song_pin_out[i]) cudaFreeHost(e->song_pin_out[i]);
     if (e->song_ev_in[i]) cudaEventDestroy(e->song_ev_in[i]);
     if (e->song_ev_out[i]) cudaEventDestroy(e->song_ev_out[i]);
+    if (e->song_ev_reg[i]) cudaEventDestroy(e->song_ev_reg[i]);
+    cudaFree(e->song_fin[i]);
   }
-  cudaFree(e->song_fin);
+  if (e->song_copy) cudaStreamDestroy(e->song_copy);
   cudaFree(e->song_strip_out);
   cudaFree(e->song_strip_in);
   if (e->graph) cudaGraphExecDestroy(e->graph);
@@ -1309,7 +1315,7 @@ int ensure_song_buffers(lbrr_engine* e, const SongGeom& g) {
   const size_t in_b = static_cast<size_t>(g.C) * 2 * sizeof(float);
   const size_t out_b = static_cast<size_t>(g.C) * 2 * kStems * sizeof(float);
   const size_t strip_b = static_cast<size_t>(2 * kStems + 1) * g.ov * sizeof(float);
-  if (!e->song_fin) {
+  if (!e->song_fin[0]) {
     // sized for the largest chunk this engine takes
     const size_t max_in = static_cast<size_t>(e->max_len) * 2 * sizeof(float);
     const size_t max_out = static_cast<size_t>(e->max_len) * 2 * kStems * sizeof(float);
@@ -1319,8 +1325,10 @@ int ensure_song_buffers(lbrr_engine* e, const SongGeom& g) {
       CK(cudaMallocHost(&e->song_pin_out[i], max_out));
       CK(cudaEventCreateWithFlags(&e->song_ev_in[i], cudaEventDisableTiming));
       CK(cudaEventCreateWithFlags(&e->song_ev_out[i], cudaEventDisableTiming));
+      CK(cudaEventCreateWithFlags(&e->song_ev_reg[i], cudaEventDisableTiming));
+      CK(cudaMalloc(&e->song_fin[i], max_out));
     }
-    CK(cudaMalloc(&e->song_fin, max_out));
+    CK(cudaStreamCreateWithFlags(&e->song_copy, cudaStreamNonBlocking));
     CK(cudaMalloc(&e->song_strip_out, max_strip));
   }
   (void)in_b;
@@ -1425,16 +1433,24 @@ void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, fl
       strip_prev = e->song_strip_in + static_cast<size_t>(c - 1) * (strip_b / sizeof(float));
     }
     if (nreg > 0) {
+      // region buffer `slot` is free once its download two chunks ago is done
+      if (cudaStreamWaitEvent(e->stream, e->song_ev_out[slot], 0) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "region buffer wait"));
       song_region_kernel<<<static_cast<unsigned>((nreg + 255) / 256), 256, 0, e->stream>>>(
-          e->dev_out, strip_prev, e->song_fin, g, c, r0, nreg, head);
+          e->dev_out, strip_prev, e->song_fin[slot], g, c, r0, nreg, head);
       if (cudaGetLastError() != cudaSuccess) return bail(fail(LBRR_ERR_CUDA, "region launch"));
     }
     // the host copy of the previous region overlaps this chunk's GPU work
     if (int rc = scatter()) return bail(rc);
     if (nreg > 0) {
-      if (cudaMemcpyAsync(e->song_pin_out[slot], e->song_fin, static_cast<size_t>(nreg) * 2 * kStems * sizeof(float),
-                          cudaMemcpyDeviceToHost, e->stream) != cudaSuccess ||
-          cudaEventRecord(e->song_ev_out[slot], e->stream) != cudaSuccess)
+      // the download runs on the copy stream, so the next chunk's forward on
+      // the compute stream does not wait for it
+      if (cudaEventRecord(e->song_ev_reg[slot], e->stream) != cudaSuccess ||
+          cudaStreamWaitEvent(e->song_copy, e->song_ev_reg[slot], 0) != cudaSuccess ||
+          cudaMemcpyAsync(e->song_pin_out[slot], e->song_fin[slot],
+                          static_cast<size_t>(nreg) * 2 * kStems * sizeof(float), cudaMemcpyDeviceToHost,
+                          e->song_copy) != cudaSuccess ||
+          cudaEventRecord(e->song_ev_out[slot], e->song_copy) != cudaSuccess)
         return bail(fail(LBRR_ERR_CUDA, "region download"));
       pend_slot = slot;
       pend_o0 = o0;
