@@ -10,7 +10,9 @@
  * Conventions (modelled on the reference's own C shim,
  * tools/cudnn_sdpa_wrap.cpp:149-168, :226-244): opaque handles, int status
  * (0 = OK, negative = error), a thread-local last-error string, all device
- * work ordered on one stream per engine.  No function aborts or exits.
+ * work ordered on one stream per engine.  No function aborts or exits.  An
+ * engine serves one host thread at a time; different engines may be driven
+ * from different threads concurrently.
  * Plain pointers and sizes only; `stream` is a cudaStream_t passed as void*.
  *
  * Layouts at the boundary (src/main.rs:7283, :7739, src/benchmark.rs:93):
@@ -114,8 +116,9 @@ int lbrr_check_safetensors(const char* path);
 int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);
 
 /* End to end from host memory: stage x_host through pinned memory, copy to
- * the device, forward, copy the stems back in slices (host threads move each
- * slice into stems_host as it arrives), synchronise, check the device status.
+ * the device, forward, copy the stems back in slices (the engine's four host
+ * copy threads, started by its first call of this function, move each slice
+ * into stems_host as it arrives), synchronise, check the device status.
  * Replaces bench_forward plus the D2H of src/main.rs:7303-7317.
  * x_host: [len][2], stems_host: [6][2][len]. */
 int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, float* stems_host);
