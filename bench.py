@@ -17,7 +17,7 @@ roofline    dominant kernel (time-axis attention) timed live on its own stream
             with CUDA events at full size: algorithmic FLOP / duration vs the
             measured dense tensor peak in MEASURED_PEAKS.json
 cpu_baseline  the CPU oracle (PyTorch fp32 restatement; the reference has no
-            CPU path) on a bounded sample, extrapolated to one chunk
+            CPU path): one whole 12-layer chunk, timed end to end on the host cores
 song        whole-song RTF (180.48 s, reference chunk plan)
             at N GPUs through lbrr_separate_song: chunks dealt round-robin,
             overlap strips exchanged between neighbouring chunks' GPUs, each GPU
@@ -44,11 +44,20 @@ CHUNK = 588800
 SONG_LEN = 7959168  # 180.48 s at 44.1 kHz
 SR = 44100
 METRIC = "ms/588800-sample chunk"
-# this repository's kernels per chunk forward: frames, band_norm, band-split GEMM,
-# 24 x (QKV, attention, out-proj, fused FF), mask GEMM1, mask GEMM2, ISTFT
-# (the two cuFFT executions are library kernels and not counted)
-LAUNCHES_PER_CHUNK = 3 + 24 * 4 + 3
 UNIT = "ms/chunk"
+# the reference's published number for this metric (RTX 3080, README.md:17 of the reference)
+PUBLISHED_MS = 157.89
+WORKLOAD = "full chunk 588800 samples (T=1151, M=71362), 12 layers, 6 stems, waveform out"
+FULL_FLOP = 6069010774016   # src/benchmark.rs:105-117 of the reference
+SHORT_FLOP = 1013639108608
+MASK_FLOP = 340460000000     # MaskEstimator, 6 stems (src/benchmark.rs:115)
+
+
+def bench_config(world):
+    """The config both arms report (identical, so the driver can pair them)."""
+    return {"workload": WORKLOAD, "global_batch": world, "seq_len": 1151,
+            "parallelism": f"chunks dealt over {world} device(s)",
+            "l2": "flushed between steps (256 MiB write outside the timed events)"}
 
 
 def peaks():
@@ -159,8 +168,9 @@ def time_dominant_kernel(torch, lbrr, T=1151, iters=10):
 
 
 def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
-    """Per-kernel tensor throughput at M = 62*T of the trunk GEMMs the forward
-    runs: QKV, out-projection and the fused feed-forward (FF1 -> GELU -> FF2)."""
+    """per-kernel tensor throughput at M = 62*T of the trunk
+    GEMMs -- QKV (+bias+RoPE), out-projection (+residual+norm), FF1 (+GELU),
+    FF2 (+residual) -- and the fused feed-forward the forward actually runs."""
     M = T * 62
     g = torch.Generator(device="cuda").manual_seed(1)
     h = torch.randn(M, 256, device="cuda", generator=g).half()
@@ -180,9 +190,12 @@ def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
     b1 = torch.zeros(1024, device="cuda")
     w2 = (torch.randn(256, 1024, device="cuda", generator=g) * 0.02).half()
     xo = torch.empty(M, 256, device="cuda")
+    f1 = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
     cases = {
         "qkv": (lambda s: lbrr.qkv_rope(h, w_qkv, b16, cos, sin, qkv, T, 62, 0, stream=s), 2 * M * 1536 * 256),
         "out_proj": (lambda s: lbrr.outproj_norm(sc, wo, bo, x, gam, ao, h2, stream=s), 2 * M * 256 * 512),
+        "ff1_gelu": (lambda s: lbrr.ff1_gelu(h, w1, b1, f1, stream=s), 2 * M * 1024 * 256),
+        "ff2_resid": (lambda s: lbrr.ff2_resid(f1, w2, bo, x, xo, stream=s), 2 * M * 256 * 1024),
         "feed_forward": (lambda s: lbrr.feed_forward(h, w1, b1, w2, bo, x, xo, stream=s), 2 * 2 * M * 1024 * 256),
     }
     res = {}
@@ -254,6 +267,7 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize()
         barrier()
     eng.sync()
+    kernels_per_chunk = eng.get_option(lbrr.INFO_KERNELS_PER_FORWARD)
     step_ms = [a.elapsed_time(b) for a, b in evs]
     ms = sum(step_ms) / len(step_ms)
     if dist:
@@ -289,23 +303,32 @@ def run_ours(args, rank, world, local_rank):
             traffic = json.loads(tf.read_text()).get("bytes_per_launch")
         for g in gemms.values():
             g["pct_of_peak"] = round(100.0 * g["tflops"] / pk["tflops"], 1)
+        mask = time_mask_estimator(torch, eng, x, out, stream, flush, args)
+        short = time_short_chunk(torch, eng, stream, flush, args)
         wb, sb = eng.memory()
         result = {
             "metric": METRIC, "value": round(ms / world, 4), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": round(ms / world / PUBLISHED_MS, 6),
+            "vs_baseline_source": f"value / {PUBLISHED_MS} ms, the reference's published full-chunk time (RTX 3080)",
             "dtype": "f16", "data": "synthetic (seeded sines + noise; random-init weights N(0,0.02))",
-            "config": {"workload": "full chunk 588800 samples (T=1151, M=71362), 12 layers, 6 stems, waveform out",
-                       "global_batch": world, "seq_len": 1151, "parallelism": f"chunks dealt over {world} GPU(s)",
-                       "l2": "flushed between steps (256 MiB write outside the timed events)"},
+            "config": bench_config(world),
             "e2e": {"value": round(e2e_ms / world, 4), "unit": UNIT, "h2d_bytes_per_step": CHUNK * 2 * 4 * world,
                     "d2h_bytes_per_step": 6 * 2 * CHUNK * 4 * world},
-            "gpu_launches": LAUNCHES_PER_CHUNK * args.steps * world,
+            "gpu_launches": kernels_per_chunk * args.steps * world,
+            "gpu_launches_source": f"{kernels_per_chunk} kernels of this library per chunk forward (counted by the "
+                                   "engine's launchers) x steps x GPUs; cuFFT's kernels not counted",
             "roofline": {"kernel": "attention time axis (attn_time_kernel, T=1151, 496 sequences)", "bound": "tensor",
                          "achieved": round(achieved, 1), "peak": pk["tflops"], "unit": "TFLOP/s",
                          "frac": round(achieved / pk["tflops"], 4), "traffic": traffic,
+                         "traffic_source": "committed ncu capture of the same launch (dram__bytes_read.sum + "
+                                           "dram__bytes_write.sum), profiles/attn_time_T1151_traffic.json",
                          "peak_source": pk["source"] + " dense bf16 burst (MEASURED_PEAKS.json)"},
+            "chunk_tflops": round(FULL_FLOP / ms / 1e9, 1),
             "trunk_gemms": gemms,
+            "short_chunk": short,
+            "mask_estimator": mask,
             "chunk_rtf": round(ms / (CHUNK / SR * 1000.0), 6),
             "song": song,
             "clocks": clocks,
@@ -318,6 +341,48 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
         dist.destroy_process_group()
     return result
+
+
+def _time_steps(torch, fn, stream, flush, steps, warmup):
+    """Mean CUDA-event ms of fn() on `stream`, L2 flushed between steps."""
+    with torch.cuda.stream(stream):
+        for _ in range(warmup):
+            fn()
+        stream.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+        for a, b in evs:
+            a.record(stream)
+            fn()
+            b.record(stream)
+            flush.fill_(1.0)
+        stream.synchronize()
+    return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+
+def time_mask_estimator(torch, eng, x, out, stream, flush, args):
+    """the back end of the full chunk alone (both grouped
+    mask GEMMs with tanh / GLU / complex mask fused, then C2R and overlap-add),
+    rerun from the last forward's final-norm output."""
+    eng.bench_forward(x, out, stream=stream)
+    ms = _time_steps(torch, lambda: eng.forward_back(out, stream=stream), stream, flush, min(args.steps, 20), 3)
+    eng.sync()
+    return {"ms": round(ms, 4), "tflops": round(MASK_FLOP / ms / 1e9, 1),
+            "scope": "mask GEMM1 (256->1024, tanh) + mask GEMM2 (1024->8200, GLU, mask apply) for 6 stems x 62 bands "
+                     "at T=1151, plus the C2R and overlap-add that follow (about 0.09 ms)"}
+
+
+def time_short_chunk(torch, eng, stream, flush, args):
+    """the 132300-sample chunk (T=259) on the device."""
+    from lbrr import synthetic
+    L = 132300
+    a = synthetic.audio(L, seed=3)
+    xs = torch.from_numpy(np.ascontiguousarray(a.T)).cuda()
+    outs = torch.empty(6, 2, L, device="cuda")
+    ms = _time_steps(torch, lambda: eng.bench_forward(xs, outs, stream=stream), stream, flush,
+                     min(args.steps, 20), 3)
+    eng.sync()
+    return {"ms": round(ms, 4), "tflops": round(SHORT_FLOP / ms / 1e9, 1), "samples": L, "frames": 259,
+            "published_rtx3080_ms": 33.81}
 
 
 def run_song(torch, lbrr, eng, rank, world, dist, cpu_group=None):
@@ -372,66 +437,61 @@ def run_song(torch, lbrr, eng, rank, world, dist, cpu_group=None):
 # ---------------------------------------------------------------------------
 # CPU baseline (oracle port) and the reference arm
 # ---------------------------------------------------------------------------
-def cpu_sample_ms(torch):
-    """Front end + one layer (time + freq axis) + mask estimator + ISTFT of the full
-    chunk on the CPU oracle in fp32; returns ms extrapolated to the 12-layer chunk."""
+def cpu_chunk_ms(torch, o, audio):
+    """One whole chunk through the CPU oracle in fp32 (the PyTorch restatement
+    of the reference forward): STFT, band split, 12 layers x (time, frequency)
+    axis, final norm, mask estimator, mask application, ISTFT."""
     from oracle import bsroformer_ref as R
-    w = R.make_weights(seed=0)
-    o = R.Oracle(w, "fp32")
-    audio = torch.from_numpy(R.synth_audio(CHUNK, seed=0))
-    T = R.num_frames(CHUNK)
     with torch.inference_mode():
         t0 = time.perf_counter()
-        spec = R.stft(audio)
-        x = o.band_split(R.spec_reorder(spec))
-        t1 = time.perf_counter()
-        x = o.trunk(x, T, layers=1)
-        t2 = time.perf_counter()
-        xf = R.rmsnorm(x, w["final_norm.gamma"], "left")
-        masks = o.mask_estimator(xf, T)
-        y = R.istft(o.mask_apply(spec, masks).reshape(12, T, R.FREQ_BINS), CHUNK)
-        t3 = time.perf_counter()
+        y = o.forward(audio)
+        dt = time.perf_counter() - t0
     assert torch.isfinite(y).all()
-    front_back = (t1 - t0) + (t3 - t2)
-    layer = t2 - t1
-    return (front_back + R.DEPTH * layer) * 1000.0, (t3 - t0)
+    return dt * 1000.0
+
+
+def cpu_setup(torch):
+    from oracle import bsroformer_ref as R
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    o = R.Oracle(R.make_weights(seed=0), "fp32")
+    audio = torch.from_numpy(R.synth_audio(CHUNK, seed=0))
+    with torch.inference_mode():
+        o.forward(torch.from_numpy(R.synth_audio(4096, seed=1)))  # thread pool and allocator warm
+    return o, audio, cores
+
+
+CPU_SAMPLE = ("CPU oracle fp32 (PyTorch restatement of the reference forward; the reference has no CPU path and "
+              "its GPU code needs the absent cuda-oxide toolchain): one whole 588800-sample chunk, all 12 layers, "
+              "STFT to ISTFT, timed end to end")
 
 
 def cpu_baseline_sample():
     import torch
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
-    ms, sample_s = cpu_sample_ms(torch)
-    return {"value": round(ms, 1), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"CPU oracle fp32 (PyTorch restatement of the reference forward): front end + 1 of 12 "
-                      f"layers + mask estimator + ISTFT of one 588800-sample chunk ({sample_s:.1f} s), "
-                      f"extrapolated to 12 layers"}
+    o, audio, cores = cpu_setup(torch)
+    ms = cpu_chunk_ms(torch, o, audio)
+    return {"value": round(ms, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": CPU_SAMPLE}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return None
     import torch
-    cores = os.cpu_count() or 1
-    torch.set_num_threads(cores)
+    o, audio, cores = cpu_setup(torch)
     for _ in range(args.warmup):
-        cpu_sample_ms(torch)
+        cpu_chunk_ms(torch, o, audio)
     vals = []
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        ms, sample_s = cpu_sample_ms(torch)
-        vals.append(ms)
+        vals.append(cpu_chunk_ms(torch, o, audio))
     ms = statistics.mean(vals)
     return {"impl": "reference", "metric": METRIC, "value": round(ms, 1), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": False,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "scaling": "weak", "vs_baseline": round(ms / PUBLISHED_MS, 4), "dtype": "f32",
             "data": "synthetic (seeded sines + noise; random-init weights N(0,0.02))",
-            "config": {"workload": "full chunk 588800 samples (T=1151, M=71362), 12 layers, 6 stems, waveform out",
-                       "global_batch": 1, "seq_len": 1151, "parallelism": "CPU host threads"},
+            "config": bench_config(world),
             "cpu_baseline": {"value": round(ms, 1), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": "CPU oracle fp32: front end + 1 layer + mask estimator + ISTFT per step, "
-                                       "extrapolated to 12 layers (the reference has no CPU path; its GPU code "
-                                       "needs the absent cuda-oxide toolchain)"},
+                             "sample": CPU_SAMPLE + f", {args.steps} chunks (mean)"},
             "e2e": {"value": round(ms, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": round(time.perf_counter() - t0, 1)}
 

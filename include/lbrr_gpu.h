@@ -130,6 +130,14 @@ int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, fl
 int lbrr_forward_trunk(lbrr_engine* e, const float* x_dev, int64_t len, int n_steps, float* x_out_dev,
                        void* stream);
 
+/* Back end of the chunk forward only -- mask estimator (both grouped GEMMs,
+ * tanh, GLU and the complex mask application), C2R and overlap-add -- rerun
+ * on the engine's scratch from the last forward's final-norm output and
+ * spectrum; len must equal that forward's.  Diagnostic stage boundary (the
+ * reference's mask stage, src/main.rs:7111-7160) used to time the
+ * MaskEstimator grouped GEMMs on their own. */
+int lbrr_forward_back(lbrr_engine* e, int64_t len, float* stems_dev, void* stream);
+
 /* Copy an internal buffer of the last forward to host memory (after syncing the
  * engine stream): "spec" [2][T][1025] complex64, "c2r" (masked spectra)
  * [12][T][1025] complex64, "pcm" [12][T][2048] fp32, "x" [T*62][256] fp32,
@@ -140,6 +148,39 @@ int lbrr_engine_read_buffer(lbrr_engine* e, const char* name, void* host_dst, in
 
 /* Synchronise the engine stream and check the device status word. */
 int lbrr_engine_sync(lbrr_engine* e);
+
+/* Engine options (lbrr_engine_set_option / lbrr_engine_get_option).
+ *
+ * LBRR_OPT_DC_NYQUIST_IMAG  0 (default) or 1.  The reference's mask_apply
+ *   (src/main.rs:1776-1817) multiplies every bin by the complex mask, so the
+ *   DC and Nyquist bins it hands to the C2R transform carry an imaginary part
+ *   (the mask's, times the real spectrum value).  A C2R transform is only
+ *   defined for Hermitian input, where those parts are zero, and torch.istft
+ *   (the model definition the reference's golden gate targets) drops them.  0
+ *   keeps those two bins real; 1 keeps the imaginary parts exactly as the
+ *   reference's GPU path computes them.
+ * LBRR_OPT_SONG_FAIL_CHUNK  -1 (default) or a chunk index.  Test hook of the
+ *   song entry point: this engine's host thread fails with LBRR_ERR_STATE just
+ *   before the forward of that chunk, so the abort path of lbrr_separate_song
+ *   (the other engines stop, the call returns the error) can be tested
+ *   without any device fault. */
+#define LBRR_OPT_DC_NYQUIST_IMAG 1
+#define LBRR_OPT_SONG_FAIL_CHUNK 2
+/* Read-only (lbrr_engine_get_option): kernels of this library launched by the
+ * last chunk forward (cuFFT's own kernels not counted); a replayed CUDA graph
+ * launches the same kernels. */
+#define LBRR_INFO_KERNELS_PER_FORWARD 100
+int lbrr_engine_set_option(lbrr_engine* e, int option, int64_t value);
+int lbrr_engine_get_option(const lbrr_engine* e, int option, int64_t* value);
+
+/* Test of the bounded device waits (no counterpart in the reference, whose
+ * waits are unbounded): launches on the engine stream one CTA that waits,
+ * through the same bounded mbarrier wait every pipeline kernel uses, on a
+ * barrier nothing completes, with a bound of limit_ns (1 ms .. 10 s).  No
+ * asynchronous copy or MMA is in flight, so the CTA records the timeout in
+ * the engine's status word and returns; the next lbrr_engine_sync reports
+ * LBRR_ERR_DEVICE and clears the status, and the engine stays usable. */
+int lbrr_engine_wait_probe(lbrr_engine* e, int64_t limit_ns);
 
 /* Resident bytes: weights and scratch (src/main.rs:7199-7252). */
 int lbrr_engine_memory(const lbrr_engine* e, int64_t* weight_bytes, int64_t* scratch_bytes);
@@ -213,11 +254,14 @@ int lbrr_op_sync(void* stream);
  * library a fixed device-memory budget.  The fp16 hidden activations use a
  * file-scope static device array of 8192 x 1024 halves (16 MiB, held by every
  * GPU that loads the library until exit); rows > 8192 are rejected with
- * LBRR_ERR_INVALID.  The first call on a device resolves the array's address
- * (with that device current) and should come before any stream capture.
- * Calls share the array: work of calls that overlaps on the GPU races.  The
- * call returns after its work on `stream` has finished and reports a kernel
- * status as LBRR_ERR_DEVICE.  Shapes: h16 [rows][256], w1 [1024][256],
+ * LBRR_ERR_INVALID.  The first call on a device (with that device current)
+ * resolves the array's address, loads the library's kernels on the device and
+ * sets their attributes, so it may block: make it once per device as a
+ * warm-up, outside any real-time thread.  Every call synchronises `stream`
+ * before it returns (it reads the kernels' status back and reports a nonzero
+ * one as LBRR_ERR_DEVICE), so calls cannot be recorded into a CUDA graph.  Do
+ * not call it again after cudaDeviceReset of that device.  Calls share the
+ * array: work of calls that overlaps on the GPU races.  Shapes: h16 [rows][256], w1 [1024][256],
  * b1 [1024], w2 [256][1024], b2 [256], resid and x [rows][256] fp32. */
 int lbrr_op_feed_forward_noalloc(const uint16_t* h16, const uint16_t* w1_16, const float* b1, const uint16_t* w2_16,
                                  const float* b2, const float* resid, float* x, int64_t rows, void* stream);

@@ -582,6 +582,7 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     if (e != cudaSuccess) return e;
     a.nk = (T + 127) / 128;
     // one query tile per CTA, two CTAs per SM
+    count_launch();
     attn_time_kernel<<<dim3(a.nk, nb * 8), kT1Threads, kT1Smem, st>>>(tm, a);
     return cudaGetLastError();
   }
@@ -595,6 +596,7 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int grid = n_items < 2 * sms ? n_items : 2 * sms;
+  count_launch();
   attn_freq_kernel<<<grid, kFThreads, kFSmem, st>>>(tm, a, n_items);
   return cudaGetLastError();
 }

@@ -85,13 +85,13 @@ constexpr uint32_t kSuspendHintNs = 1000000u;  // 1 ms per suspension; the phase
 // CTA-wide abort flag and the device status) when the time limit passes or
 // another thread of the CTA already gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status) {
+                                          int* status, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   for (;;) {
     if (mbar_try_wait_suspend(bar, parity, kSuspendHintNs)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       *abort_flag = 1;
       report_status(status, kDevWaitTimeout);
       return false;

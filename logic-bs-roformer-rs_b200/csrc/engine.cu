@@ -24,6 +24,8 @@
 
 using namespace lbrr;
 
+thread_local long long lbrr::t_kernel_launches = 0;
+
 // ---------------------------------------------------------------------------
 // Errors
 // ---------------------------------------------------------------------------
@@ -210,9 +212,10 @@ class HostPool {
   bool stop_ = false;
 };
 
-// Byte range [lo, hi) of worker w's share of n bytes (64-byte aligned cuts).
+// Byte range [lo, hi) of worker w's share of n bytes (64-byte aligned cuts;
+// the shares cover all n bytes whatever n mod kHostWorkers is).
 static inline void host_share(size_t n, int w, size_t& lo, size_t& hi) {
-  const size_t part = (n / kHostWorkers + 63) / 64 * 64;
+  const size_t part = ((n + kHostWorkers - 1) / kHostWorkers + 63) / 64 * 64;
   lo = std::min(n, part * static_cast<size_t>(w));
   hi = std::min(n, lo + part);
 }
@@ -283,6 +286,10 @@ struct lbrr_engine {
   // the host threads that copy them (started by the first call)
   cudaEvent_t host_ev[kHostSlices] = {};
   std::unique_ptr<HostPool> host_pool;
+  // options (lbrr_engine_set_option)
+  bool keep_dc_imag = false;     // LBRR_OPT_DC_NYQUIST_IMAG
+  int64_t song_fail_chunk = -1;  // LBRR_OPT_SONG_FAIL_CHUNK
+  int64_t kernels_per_forward = 0;  // this library's launches in the last directly issued forward
 };
 
 namespace {
@@ -874,7 +881,7 @@ static int run_back(lbrr_engine* e, int64_t len, float* out, cudaStream_t st) {
   CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, T, kStems * kNumBands, e->tiles_m1, e->n_m1, e->status,
                  st));
   CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
-                 G.n2tot, e->tiles_m2, e->n_m2, e->status, st));
+                 G.n2tot, e->tiles_m2, e->n_m2, e->keep_dc_imag, e->status, st));
   CKFFT(cufftSetStream(e->plan_c2r, st));
   CKFFT(cufftExecC2R(e->plan_c2r, reinterpret_cast<cufftComplex*>(e->c2r), e->pcm));
   CKL(istft_ola(e->pcm, e->window, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
@@ -891,10 +898,13 @@ static int check_forward_args(lbrr_engine* e, const void* x, int64_t len, const 
 }
 
 static int run_forward(lbrr_engine* e, const float* x, int64_t len, float* out, cudaStream_t st) {
+  const long long l0 = t_kernel_launches;
   if (int rc = run_front(e, x, len, st)) return rc;
   for (int k = 0; k < 2 * kDepth; ++k)
     if (int rc = run_step(e, k, st)) return rc;
-  return run_back(e, len, out, st);
+  const int rc = run_back(e, len, out, st);
+  e->kernels_per_forward = t_kernel_launches - l0;
+  return rc;
 }
 
 // The same launches captured into a graph on the caller's stream (not the
@@ -964,6 +974,15 @@ extern "C" int lbrr_forward_trunk(lbrr_engine* e, const float* x, int64_t len, i
   return LBRR_OK;
 }
 
+extern "C" int lbrr_forward_back(lbrr_engine* e, int64_t len, float* stems_dev, void* stream) {
+  if (!e || !stems_dev) return fail(LBRR_ERR_INVALID, "NULL argument");
+  if (e->cur_len <= 0) return fail(LBRR_ERR_STATE, "no forward has run yet");
+  if (len != e->cur_len) return fail(LBRR_ERR_STATE, "len differs from the last forward's");
+  DeviceGuard g(e->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+  return run_back(e, len, stems_dev, st);
+}
+
 static int check_status(int* status_dev, cudaStream_t st) {
   int h = 0;
   CK(cudaMemcpyAsync(&h, status_dev, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -1005,6 +1024,66 @@ extern "C" int lbrr_engine_sync(lbrr_engine* e) {
   DeviceGuard g(e->device);
   CK(cudaStreamSynchronize(e->stream));
   return check_status(e->status, e->stream);
+}
+
+extern "C" int lbrr_engine_set_option(lbrr_engine* e, int option, int64_t value) {
+  if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
+  switch (option) {
+    case LBRR_OPT_DC_NYQUIST_IMAG:
+      if (value != 0 && value != 1) return fail(LBRR_ERR_INVALID, "LBRR_OPT_DC_NYQUIST_IMAG takes 0 or 1");
+      if (e->keep_dc_imag != (value == 1)) {
+        DeviceGuard g(e->device);
+        CK(cudaStreamSynchronize(e->stream));
+        drop_graph(e);  // the captured launches carry the old setting
+        e->keep_dc_imag = value == 1;
+      }
+      return LBRR_OK;
+    case LBRR_OPT_SONG_FAIL_CHUNK:
+      if (value < -1) return fail(LBRR_ERR_INVALID, "LBRR_OPT_SONG_FAIL_CHUNK takes -1 or a chunk index");
+      e->song_fail_chunk = value;
+      return LBRR_OK;
+    default:
+      return fail(LBRR_ERR_INVALID, "unknown engine option " + std::to_string(option));
+  }
+}
+
+extern "C" int lbrr_engine_get_option(const lbrr_engine* e, int option, int64_t* value) {
+  if (!e || !value) return fail(LBRR_ERR_INVALID, "NULL argument");
+  switch (option) {
+    case LBRR_OPT_DC_NYQUIST_IMAG: *value = e->keep_dc_imag ? 1 : 0; return LBRR_OK;
+    case LBRR_OPT_SONG_FAIL_CHUNK: *value = e->song_fail_chunk; return LBRR_OK;
+    case LBRR_INFO_KERNELS_PER_FORWARD: *value = e->kernels_per_forward; return LBRR_OK;
+    default: return fail(LBRR_ERR_INVALID, "unknown engine option " + std::to_string(option));
+  }
+}
+
+// One CTA waits, through the bounded mbarrier wait every pipeline kernel uses,
+// on a barrier whose phase nothing completes.  Nothing asynchronous is issued,
+// so when the limit passes the CTA only records the timeout and returns.
+__global__ void wait_probe_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, status, limit_ns);
+    if (ok) report_status(status, kDevSmemMisaligned);  // cannot happen: nothing arrives
+  }
+  __syncthreads();
+}
+
+extern "C" int lbrr_engine_wait_probe(lbrr_engine* e, int64_t limit_ns) {
+  if (!e) return fail(LBRR_ERR_INVALID, "engine is NULL");
+  if (limit_ns < 1000000 || limit_ns > 10000000000ll)
+    return fail(LBRR_ERR_INVALID, "limit_ns must be in [1 ms, 10 s]");
+  DeviceGuard g(e->device);
+  wait_probe_kernel<<<1, 32, 0, e->stream>>>(e->status, static_cast<unsigned long long>(limit_ns));
+  CK(cudaGetLastError());
+  return LBRR_OK;
 }
 
 // The stems leave the GPU in kHostSlices slices, each followed by an event;
@@ -1179,6 +1258,10 @@ static int separate_song_serial(lbrr_engine* const* engines, int n, const float*
       std::memcpy(e->pin_in, xp.data() + 2 * s, static_cast<size_t>(C) * 2 * sizeof(float));
       if (cudaMemcpyAsync(e->dev_in, e->pin_in, static_cast<size_t>(C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
                           e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "H2D chunk"); break; }
+      if (e->song_fail_chunk == static_cast<int64_t>(ci)) {  // host-side failure injection
+        rc = fail(LBRR_ERR_STATE, "injected failure before the forward of chunk " + std::to_string(ci));
+        break;
+      }
       if ((rc = lbrr_forward_chunk(e, e->dev_in, C, e->dev_out, e->stream)) != LBRR_OK) break;
       if (cudaEventRecord(ev_done[slot], e->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "event record"); break; }
     }
@@ -1398,6 +1481,8 @@ void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, fl
                         e->stream) != cudaSuccess ||
         cudaEventRecord(e->song_ev_in[slot], e->stream) != cudaSuccess)
       return bail(fail(LBRR_ERR_CUDA, "chunk upload"));
+    if (e->song_fail_chunk == c)  // host-side failure injection (tests of the abort path)
+      return bail(fail(LBRR_ERR_STATE, "injected failure before the forward of chunk " + std::to_string(c)));
     if (int rc = lbrr_forward_chunk(e, e->dev_in, g.C, e->dev_out, e->stream)) return bail(rc);
     const unsigned blocks_ov = static_cast<unsigned>((g.ov + 255) / 256);
     if (c + 1 < g.nc) {

@@ -747,6 +747,7 @@ struct EpiMask : TableTiles {
   const float2* spec;   // [2][T][1025]
   float2* out;          // [stems*2][T][1025]
   int T, n2tot;
+  int keep_dc_imag;     // 1: the DC/Nyquist bins keep the imaginary part the complex mask gives them
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const bool valid = x.row < t.rows;
     const int rb = x.q * 32;                // this warp's first tile row
@@ -804,9 +805,11 @@ struct EpiMask : TableTiles {
             float2 o;
             o.x = sp.x * mr - sp.y * mi;
             // A real signal's DC and Nyquist bins are real: torch.istft drops
-            // their imaginary parts, and cuFFT's C2R is only defined for such
-            // Hermitian input, so the masked spectrum keeps them real.
-            o.y = (f == 0 || f == 1024) ? 0.f : sp.x * mi + sp.y * mr;
+            // their imaginary parts, and a C2R transform is only defined for
+            // such Hermitian input, so by default the masked spectrum keeps
+            // them real.  keep_dc_imag reproduces the reference's mask_apply
+            // (src/main.rs:1776-1817), which passes them on unchanged.
+            o.y = ((f == 0 || f == 1024) && !keep_dc_imag) ? 0.f : sp.x * mi + sp.y * mr;
             slot = o;
           }
         }
@@ -1310,6 +1313,7 @@ static cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& b, const
   if (e != cudaSuccess) return e;
   if (tiles <= 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
+  count_launch();
   gemm_tc_kernel<Epi><<<grid, kGemmThreads, kGemmSmem, st>>>(a, b, epi, tiles, status);
   return cudaGetLastError();
 }
@@ -1458,6 +1462,7 @@ cudaError_t gemm_ff_fused(const __half* h16, const __half* w1, const float* b1, 
   const int tiles = dense_tiles(M, 256);
   if (tiles <= 0) return cudaSuccess;
   const int grid = tiles < num_sms() ? tiles : num_sms();
+  count_launch();
   ff_fused_kernel<<<grid, kFfThreads, kFfSmem, st>>>(th, tw1, tw2, ep, b1, tiles, status);
   return cudaGetLastError();
 }
@@ -1504,7 +1509,8 @@ cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __
 
 cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, const int* band_f0,
                        const int* band_d, const int* band_o2, const float2* spec, float2* c2r, int T, int stems,
-                       int n2tot, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st) {
+                       int n2tot, const TileDesc* tiles, int n_tiles, bool keep_dc_imag, int* status,
+                       cudaStream_t st) {
   CUtensorMap ta, tb;
   cudaError_t e = make_map_2d(&ta, hidden, 1024, static_cast<uint64_t>(T) * kNumBands * stems, 1024 * 2, kBK, kBM);
   if (e == cudaSuccess)
@@ -1520,6 +1526,7 @@ cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, 
   ep.out = c2r;
   ep.T = T;
   ep.n2tot = n2tot;
+  ep.keep_dc_imag = keep_dc_imag ? 1 : 0;
   return launch_gemm(ta, tb, ep, n_tiles, status, st);
 }
 

@@ -11,6 +11,11 @@ extern "C" int lbrr_set_error_for_host(int code, const char* msg);
 
 namespace lbrr {
 
+// Kernel launches issued by this library from the calling thread; the engine
+// takes the difference around one forward to report its launches per chunk.
+extern thread_local long long t_kernel_launches;
+inline void count_launch() { ++t_kernel_launches; }
+
 constexpr int kNumBands = 62;
 constexpr int kDim = 256;
 constexpr int kHeads = 8;
@@ -72,7 +77,8 @@ cudaError_t gemm_mask1(const __half* xb16, const __half* w1, const float* b1, __
                        const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
 cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, const int* band_f0,
                        const int* band_d, const int* band_o2, const float2* spec, float2* c2r, int T, int stems,
-                       int n2tot, const TileDesc* tiles, int n_tiles, int* status, cudaStream_t st);
+                       int n2tot, const TileDesc* tiles, int n_tiles, bool keep_dc_imag, int* status,
+                       cudaStream_t st);
 
 // ---- attention (attention.cu) ----------------------------------------------
 cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,

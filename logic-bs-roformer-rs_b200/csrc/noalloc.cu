@@ -5,19 +5,27 @@
 //
 // lbrr_op_feed_forward_noalloc runs FF1 + GELU into a file-scope scratch array
 // and then FF2 + bias + residual (the FF part of transformer_step,
-// src/main.rs:6234-6259, with the engine's ff1 intermediate).  Nothing is
-// allocated at call time:
+// src/main.rs:6234-6259, with the engine's ff1 intermediate).  No call
+// allocates device memory:
 //   * the fp16 hidden activations live in g_ff1_scratch, a static array of
 //     kNoAllocMaxRows x 1024 halves (16 MiB) that every GPU loading this
 //     library holds until the process exits; larger row counts are rejected;
 //   * the kernels' status words live in g_ff_status.
 // In host code these array names are host-side stand-ins, not device
 // addresses: the first call on a device (with that device current) resolves
-// their device addresses with cudaGetSymbolAddress and caches them, so that
-// first call should come before any stream capture.  All calls share the
-// arrays and leave the last call's contents behind; calls whose work overlaps
-// on the GPU (different streams, or threads racing on one device) race on the
-// scratch and must be serialised by the caller.
+// their device addresses with cudaGetSymbolAddress and caches them.  That
+// first call also makes the CUDA runtime load this library's module on the
+// device (which is when the 16 MiB array comes into existence under lazy
+// module loading) and sets the GEMM kernels' shared-memory attributes, so it
+// can block: make it once per device as a warm-up, outside the real-time
+// thread.  Every call ends by synchronising `stream` (it reads the kernels'
+// status back), so a call cannot be recorded into a CUDA graph.  The cached
+// addresses belong to the device's current primary context: after
+// cudaDeviceReset on that device this entry point must not be called again in
+// the process.  All calls share the arrays and leave the last call's contents
+// behind; calls whose work overlaps on the GPU (different streams, or threads
+// racing on one device) race on the scratch and must be serialised by the
+// caller.
 #include <mutex>
 #include <string>
 

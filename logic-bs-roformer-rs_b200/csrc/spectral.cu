@@ -93,6 +93,7 @@ __global__ void frames_kernel(const float* __restrict__ x, const float* __restri
 cudaError_t stft_frames(const float* x, const float* window, float* frames, int len, int T, cudaStream_t st) {
   const long long total4 = 2ll * T * (kNfft / 4);
   const int threads = 256;
+  count_launch();
   frames_kernel<<<static_cast<unsigned>((total4 + threads - 1) / threads), threads, 0, st>>>(x, window, frames, len,
                                                                                               T);
   return cudaGetLastError();
@@ -146,6 +147,7 @@ __global__ void band_norm_kernel(const float2* __restrict__ spec, const float* _
 cudaError_t band_norm(const float2* spec, const float* gamma, const int* band_tab, __half* xn, int xn_cols, int T,
                       int nb, cudaStream_t st) {
   const long long threads_total = static_cast<long long>(T) * nb * 32;
+  count_launch();
   band_norm_kernel<<<static_cast<unsigned>((threads_total + 255) / 256), 256, 0, st>>>(spec, gamma, band_tab, xn,
                                                                                         xn_cols, T, nb);
   return cudaGetLastError();
@@ -196,6 +198,7 @@ __global__ void __launch_bounds__(512) norm_gates_kernel(const float* __restrict
 cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, const float* gate_b, __half* h16,
                        float* gates, int rows, cudaStream_t st) {
   const int warps = 16;
+  count_launch();
   norm_gates_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(x, gamma, gate_w, gate_b, h16, gates, rows);
   return cudaGetLastError();
 }
@@ -224,6 +227,7 @@ __global__ void istft_kernel(const float* __restrict__ pcm, const float* __restr
 cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_env, float* out, int len, int T,
                       int channels, cudaStream_t st) {
   const long long n = static_cast<long long>(channels) * len;
+  count_launch();
   istft_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, st>>>(pcm, window, inv_env, out, len, T, channels);
   return cudaGetLastError();
 }

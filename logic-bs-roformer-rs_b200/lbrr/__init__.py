@@ -75,7 +75,11 @@ def lib() -> C.CDLL:
         "lbrr_forward_chunk": ([vp, vp, i64, vp, vp], C.c_int),
         "lbrr_forward_chunk_host": ([vp, vp, i64, vp], C.c_int),
         "lbrr_forward_trunk": ([vp, vp, i64, C.c_int, vp, vp], C.c_int),
+        "lbrr_forward_back": ([vp, i64, vp, vp], C.c_int),
         "lbrr_engine_sync": ([vp], C.c_int),
+        "lbrr_engine_set_option": ([vp, C.c_int, i64], C.c_int),
+        "lbrr_engine_get_option": ([vp, C.c_int, C.POINTER(i64)], C.c_int),
+        "lbrr_engine_wait_probe": ([vp, i64], C.c_int),
         "lbrr_engine_read_buffer": ([vp, C.c_char_p, vp, i64], C.c_int),
         "lbrr_engine_memory": ([vp, C.POINTER(i64), C.POINTER(i64)], C.c_int),
         "lbrr_engine_destroy": ([vp], None),
@@ -103,7 +107,9 @@ def lib() -> C.CDLL:
 HEADER_SYMBOLS = [
     "lbrr_last_error", "lbrr_abi_version", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
     "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
-    "lbrr_engine_sync", "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
+    "lbrr_forward_back",
+    "lbrr_engine_sync", "lbrr_engine_set_option", "lbrr_engine_get_option", "lbrr_engine_wait_probe",
+    "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
     "lbrr_op_qkv_rope", "lbrr_op_attention", "lbrr_op_outproj_norm", "lbrr_op_ff1_gelu", "lbrr_op_ff2_resid",
     "lbrr_op_feed_forward", "lbrr_op_sync", "lbrr_op_feed_forward_noalloc",
 ]
@@ -122,6 +128,11 @@ def _ptr(t):
         return t.ctypes.data
     return t.data_ptr()
 
+
+# engine options (include/lbrr_gpu.h)
+OPT_DC_NYQUIST_IMAG = 1
+OPT_SONG_FAIL_CHUNK = 2
+INFO_KERNELS_PER_FORWARD = 100
 
 CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream named explicitly
 
@@ -211,8 +222,25 @@ class Engine:
         length = x_dev.numel() // 2
         check(lib().lbrr_forward_trunk(self.handle, _ptr(x_dev), length, n_steps, _ptr(x_out_dev), _stream(stream)))
 
+    def forward_back(self, out_dev, stream=None):
+        """Rerun the back end (mask estimator -> ISTFT) of the last forward."""
+        length = out_dev.numel() // 12
+        check(lib().lbrr_forward_back(self.handle, length, _ptr(out_dev), _stream(stream)))
+
     def sync(self):
         check(lib().lbrr_engine_sync(self.handle))
+
+    def set_option(self, option: int, value: int):
+        check(lib().lbrr_engine_set_option(self.handle, option, value))
+
+    def get_option(self, option: int) -> int:
+        v = C.c_int64()
+        check(lib().lbrr_engine_get_option(self.handle, option, C.byref(v)))
+        return v.value
+
+    def wait_probe(self, limit_ns: int):
+        """Launch the bounded-wait probe (a wait nothing ends, bounded by limit_ns)."""
+        check(lib().lbrr_engine_wait_probe(self.handle, limit_ns))
 
     def read_buffer(self, name: str, shape, dtype) -> np.ndarray:
         """Host copy of an internal buffer of the last forward (diagnostic tap)."""

@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in this directory from the reference's own code.
 
-Run in a container where the reference tree is mounted (default path below, or
-``--reference DIR``).  Two reference modules are imported and executed:
+Run with ``--reference DIR`` naming a checkout of the reference repository
+(read-only).  Two reference modules are imported and executed:
 
 * ``tools/dump_refs.py`` -- the reference's seeded per-op parity generators
   (torch CPU): STFT, RMSNorm, band-split, the four trunk GEMM shapes, QKV+RoPE,
@@ -110,7 +110,8 @@ def demix_identity(ref: Path) -> dict:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", type=Path, default=Path("/root/reference"))
+    ap.add_argument("--reference", type=Path, required=True,
+                    help="root of a checkout of the reference repository (read-only)")
     a = ap.parse_args()
     np.savez_compressed(HERE / "dump_refs_subset.npz", **dump_refs_subset(a.reference))
     np.savez_compressed(HERE / "demix_identity.npz", **demix_identity(a.reference))

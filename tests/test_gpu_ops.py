@@ -67,7 +67,8 @@ def test_qkv_rope(lb, T, axis, nb):
         assert float((got[:, sl] - r).abs().max()) <= 4e-3 * float(r.abs().max())
 
 
-@pytest.mark.parametrize("T,axis", [(1, 0), (37, 0), (129, 0), (200, 0), (259, 0), (300, 0), (1, 1), (2, 1), (37, 1)])
+@pytest.mark.parametrize("T,axis", [(1, 0), (37, 0), (129, 0), (200, 0), (259, 0), (300, 0), (1151, 0), (1, 1), (2, 1),
+                                    (37, 1), (1151, 1)])
 def test_attention(lb, T, axis):
     M = T * NB
     qkv = f16(randn((M, 1536), 20 + T, 1.0))
