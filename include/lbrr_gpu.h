@@ -170,6 +170,16 @@ int lbrr_engine_sync(lbrr_engine* e);
  * last chunk forward (cuFFT's own kernels not counted); a replayed CUDA graph
  * launches the same kernels. */
 #define LBRR_INFO_KERNELS_PER_FORWARD 100
+/* Read-only: host-side phase times, in microseconds, of the last weight load
+ * (file read and header parse, both 0 for lbrr_engine_load_weights; validation
+ * plus fp16 packing; the host-to-device copy) and of the last per-length setup
+ * (RoPE and tile tables, FFT plans, ISTFT envelope), as the reference's
+ * --bench JSON reports them (timing_ms, src/main.rs:7339-7343). */
+#define LBRR_INFO_WEIGHTS_READ_US 101
+#define LBRR_INFO_WEIGHTS_PARSE_US 102
+#define LBRR_INFO_WEIGHTS_PACK_US 103
+#define LBRR_INFO_WEIGHTS_H2D_US 104
+#define LBRR_INFO_SETUP_US 105
 int lbrr_engine_set_option(lbrr_engine* e, int option, int64_t value);
 int lbrr_engine_get_option(const lbrr_engine* e, int option, int64_t* value);
 

@@ -71,6 +71,19 @@ def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
     return LIB
 
 
+def source_sha256() -> str:
+    """SHA256 over the library, CLI and header sources (sorted by path), embedded
+    in the CLI binary for its --bench identity record."""
+    import hashlib
+    h = hashlib.sha256()
+    files = sorted(list(CSRC.glob("*")) + list(HOST.glob("*")) + list(INCLUDE.glob("*.h")))
+    for f in files:
+        if f.is_file():
+            h.update(f.name.encode())
+            h.update(f.read_bytes())
+    return h.hexdigest()
+
+
 def build_cli(verbose: bool = False) -> Path:
     """The host command-line front end (host/*.cpp), linked against the engine
     library it sits next to (rpath $ORIGIN) and the CUDA runtime."""
@@ -78,7 +91,8 @@ def build_cli(verbose: bool = False) -> Path:
     deps = srcs + sorted(HOST.glob("*.h")) + [LIB, INCLUDE / "lbrr_gpu.h"]
     if CLI.exists() and CLI.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
         return CLI
-    cmd = [CXX, "-O2", "-std=c++17", "-Wall", "-I", str(CUDA_HOME / "include"), *map(str, srcs), "-o", str(CLI),
+    cmd = [CXX, "-O2", "-std=c++17", "-Wall", f'-DLBRR_SOURCE_SHA256="{source_sha256()}"',
+           "-I", str(CUDA_HOME / "include"), *map(str, srcs), "-o", str(CLI),
            "-L", str(LIB.parent), "-llbrr_b200", "-L", str(CUDA_HOME / "lib64"), "-lcudart", "-lpthread",
            "-Wl,-rpath,$ORIGIN"]
     if verbose:

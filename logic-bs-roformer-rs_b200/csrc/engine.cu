@@ -290,7 +290,21 @@ struct lbrr_engine {
   bool keep_dc_imag = false;     // LBRR_OPT_DC_NYQUIST_IMAG
   int64_t song_fail_chunk = -1;  // LBRR_OPT_SONG_FAIL_CHUNK
   int64_t kernels_per_forward = 0;  // this library's launches in the last directly issued forward
+  // host-side phase times of the last weight load and per-length setup (microseconds)
+  int64_t us_read = 0, us_parse = 0, us_pack = 0, us_h2d = 0, us_setup = 0;
 };
+
+static int64_t us_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration_cast<std::chrono::microseconds>(std::chrono::steady_clock::now() - t0).count();
+}
+
+// Called by the safetensors reader (safetensors.cpp) with the file-read and
+// header-parse times of the load it is about to hand to lbrr_engine_load_weights.
+extern "C" void lbrr_engine_note_file_times(lbrr_engine* e, int64_t us_read, int64_t us_parse) {
+  if (!e) return;
+  e->us_read = us_read;
+  e->us_parse = us_parse;
+}
 
 namespace {
 struct DeviceGuard {
@@ -687,9 +701,14 @@ static int build_weight_image(const lbrr_engine* e, const char* base, const lbrr
 extern "C" int lbrr_engine_load_weights(lbrr_engine* e, const lbrr_weight_view* views, size_t n) {
   if (!e) return fail(LBRR_ERR_INVALID, "NULL engine");
   std::vector<uint8_t> host;
+  e->us_read = e->us_parse = 0;
+  auto t0 = std::chrono::steady_clock::now();
   if (int rc = build_weight_image(e, static_cast<const char*>(e->warena), views, n, host)) return rc;
+  e->us_pack = us_since(t0);
   DeviceGuard g(e->device);
+  t0 = std::chrono::steady_clock::now();
   CK(cudaMemcpy(e->warena, host.data(), host.size(), cudaMemcpyHostToDevice));
+  e->us_h2d = us_since(t0);
   e->weights_loaded = true;
   return LBRR_OK;
 }
@@ -723,8 +742,16 @@ static void drop_graph(lbrr_engine* e) {
   e->graph_len = -1;
 }
 
+static int setup_length_impl(lbrr_engine* e, int64_t len);
 static int setup_length(lbrr_engine* e, int64_t len) {
   if (e->cur_len == len) return LBRR_OK;
+  const auto t0 = std::chrono::steady_clock::now();
+  const int rc = setup_length_impl(e, len);
+  e->us_setup = us_since(t0);
+  return rc;
+}
+
+static int setup_length_impl(lbrr_engine* e, int64_t len) {
   drop_graph(e);  // it refers to the per-length buffers released below
   const BandGeom& G = geom();
   const int T = T_of(len);
@@ -1053,6 +1080,11 @@ extern "C" int lbrr_engine_get_option(const lbrr_engine* e, int option, int64_t*
     case LBRR_OPT_DC_NYQUIST_IMAG: *value = e->keep_dc_imag ? 1 : 0; return LBRR_OK;
     case LBRR_OPT_SONG_FAIL_CHUNK: *value = e->song_fail_chunk; return LBRR_OK;
     case LBRR_INFO_KERNELS_PER_FORWARD: *value = e->kernels_per_forward; return LBRR_OK;
+    case LBRR_INFO_WEIGHTS_READ_US: *value = e->us_read; return LBRR_OK;
+    case LBRR_INFO_WEIGHTS_PARSE_US: *value = e->us_parse; return LBRR_OK;
+    case LBRR_INFO_WEIGHTS_PACK_US: *value = e->us_pack; return LBRR_OK;
+    case LBRR_INFO_WEIGHTS_H2D_US: *value = e->us_h2d; return LBRR_OK;
+    case LBRR_INFO_SETUP_US: *value = e->us_setup; return LBRR_OK;
     default: return fail(LBRR_ERR_INVALID, "unknown engine option " + std::to_string(option));
   }
 }

@@ -4,6 +4,7 @@
 // shape, and hands fp32 views to lbrr_engine_load_weights, which validates the
 // key set.  Restates SafeTensors::open / f32_tensor / parse_header
 // (src/weights.rs:25-120) without the Rust host.
+#include <chrono>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -195,7 +196,8 @@ namespace {
 // Parse the file into fp32 buffers and name-keyed views (views point into bufs
 // and metas, which the caller keeps alive).
 int read_views(const char* path, std::vector<Meta>& metas, std::vector<std::vector<float>>& bufs,
-               std::vector<lbrr_weight_view>& views) {
+               std::vector<lbrr_weight_view>& views, int64_t* us_read = nullptr, int64_t* us_parse = nullptr) {
+  const auto t0 = std::chrono::steady_clock::now();
   FILE* f = std::fopen(path, "rb");
   if (!f) return lbrr_set_error_for_host(LBRR_ERR_WEIGHTS, (std::string("open ") + path).c_str());
   uint8_t lb[8];
@@ -231,6 +233,7 @@ int read_views(const char* path, std::vector<Meta>& metas, std::vector<std::vect
     }
   }
   std::fclose(f);
+  const auto t1 = std::chrono::steady_clock::now();
   Parser p{header.data(), header.size()};
   metas.clear();
   if (!p.header(metas)) return lbrr_set_error_for_host(LBRR_ERR_WEIGHTS, ("safetensors header: " + p.err).c_str());
@@ -251,17 +254,25 @@ int read_views(const char* path, std::vector<Meta>& metas, std::vector<std::vect
     views[k].data = bufs[k].data();
     views[k].numel = static_cast<int64_t>(numel);
   }
+  const auto t2 = std::chrono::steady_clock::now();
+  if (us_read) *us_read = std::chrono::duration_cast<std::chrono::microseconds>(t1 - t0).count();
+  if (us_parse) *us_parse = std::chrono::duration_cast<std::chrono::microseconds>(t2 - t1).count();
   return LBRR_OK;
 }
 }  // namespace
+
+extern "C" void lbrr_engine_note_file_times(lbrr_engine* e, int64_t us_read, int64_t us_parse);
 
 extern "C" int lbrr_engine_load_safetensors(lbrr_engine* e, const char* path) {
   if (!e || !path) return lbrr_set_error_for_host(LBRR_ERR_INVALID, "NULL engine or path");
   std::vector<Meta> metas;
   std::vector<std::vector<float>> bufs;
   std::vector<lbrr_weight_view> views;
-  if (int rc = read_views(path, metas, bufs, views)) return rc;
-  return lbrr_engine_load_weights(e, views.data(), views.size());
+  int64_t us_read = 0, us_parse = 0;
+  if (int rc = read_views(path, metas, bufs, views, &us_read, &us_parse)) return rc;
+  const int rc = lbrr_engine_load_weights(e, views.data(), views.size());
+  if (rc == LBRR_OK) lbrr_engine_note_file_times(e, us_read, us_parse);
+  return rc;
 }
 
 extern "C" int lbrr_check_safetensors(const char* path) {

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "../../include/lbrr_gpu.h"
+#include "bench.h"
 #include "config.h"
 #include "plan.h"
 #include "wav.h"
@@ -25,9 +26,11 @@ using namespace lbrr_host;
 namespace {
 
 struct Args {
-  std::string model_dir = "assets", input, outdir = "separated", mode, stems, bench_json;
-  int device = 0, gpus = 1, warmup = 5, iters = 20;
-  bool separate = false, dry_run = false, bench = false, print_config = false, check_weights = false;
+  std::string model_dir = "assets", input, outdir = "separated", mode, stems, bench_json, bench_ref, bench_output,
+              bench_stage = "waveform";
+  int device = 0, gpus = 1, warmup = 5, iters = 10;
+  bool separate = false, dry_run = false, bench = false, dualbench = false, kernel_regression = false,
+       print_config = false, check_weights = false;
 };
 
 void usage() {
@@ -35,7 +38,9 @@ void usage() {
                "usage: lbrr_b200 [options] --input song.wav [--outdir DIR]          separation\n"
                "       lbrr_b200 --separate --model-dir DIR --input song.wav --outdir DIR [--gpus N] [--device D]\n"
                "       lbrr_b200 --dry-run --input song.wav [--mode vocals|stems] [--stems a,b]   plan only, no GPU\n"
-               "       lbrr_b200 --bench --model-dir DIR [--warmup N --iters N --bench-json F]\n"
+               "       lbrr_b200 --bench --model-dir DIR [--warmup N --iters N --bench-stage waveform]\n"
+               "                        [--bench-ref F.npz --bench-json F --bench-output F]   (--dualbench: 2 chunks in flight)\n"
+               "       lbrr_b200 --kernel-regression [--bench-json F] [--device D]   checkpoint-free GPU checks\n"
                "       lbrr_b200 --print-config | --check-weights   (with --model-dir DIR)\n"
                "options: --mode stems|vocals, --stems all|names|indices, --device D (first GPU), --gpus N\n");
 }
@@ -88,6 +93,19 @@ int parse_args(int argc, char** argv, Args& a) {
     } else if (s == "--bench-json") {
       if (!(v = need("--bench-json"))) return 2;
       a.bench_json = v;
+    } else if (s == "--bench-ref") {
+      if (!(v = need("--bench-ref"))) return 2;
+      a.bench_ref = v;
+    } else if (s == "--bench-output") {
+      if (!(v = need("--bench-output"))) return 2;
+      a.bench_output = v;
+    } else if (s == "--bench-stage") {
+      if (!(v = need("--bench-stage"))) return 2;
+      a.bench_stage = v;
+    } else if (s == "--dualbench") {
+      a.dualbench = true;
+    } else if (s == "--kernel-regression") {
+      a.kernel_regression = true;
     } else if (s == "--separate") {
       a.separate = true;
     } else if (s == "--dry-run" || s == "--plan") {
@@ -363,98 +381,10 @@ int separate(const Args& a) {
   return 0;
 }
 
-// Device-resident chunk forward timed with CUDA events (the reference's
-// --bench, src/main.rs:7254-7362): seeded synthetic stereo, warm-up, then
-// `iters` timed forwards; prints and optionally writes a JSON line.
-int bench(const Args& a) {
-  ModelConfig c;
-  std::string err, why;
-  if (!load_model_config(a.model_dir, c, err) || !supported(c, why)) {
-    std::fprintf(stderr, "lbrr_b200: model: %s\n", err.empty() ? why.c_str() : err.c_str());
-    return 1;
-  }
-  Engines eng;
-  if (int rc = open_engines(a, 1, eng)) return rc;
-  const int64_t L = 588800;
-  std::vector<float> x(static_cast<size_t>(2 * L));
-  uint64_t st = 0x9E3779B97F4A7C15ull;
-  auto uni = [&]() {
-    st ^= st << 13;
-    st ^= st >> 7;
-    st ^= st << 17;
-    return static_cast<double>(st >> 11) * (1.0 / 9007199254740992.0);
-  };
-  for (int ch = 0; ch < 2; ++ch) {
-    double f[8], ph[8], amp[8];
-    for (int k = 0; k < 8; ++k) {
-      f[k] = 50.0 + uni() * 14950.0;
-      ph[k] = uni() * 6.283185307179586;
-      amp[k] = 0.05 + uni() * 0.1;
-    }
-    for (int64_t i = 0; i < L; ++i) {
-      double v = (uni() - 0.5) * 0.1;
-      for (int k = 0; k < 8; ++k) v += amp[k] * std::sin(6.283185307179586 * f[k] * i / 44100.0 + ph[k]);
-      x[2 * i + ch] = static_cast<float>(0.25 * v);
-    }
-  }
-  cudaSetDevice(a.device);
-  float *dx = nullptr, *dy = nullptr;
-  cudaStream_t s = nullptr;
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  int rc = 0;
-  if (cudaMalloc(&dx, x.size() * 4) != cudaSuccess || cudaMalloc(&dy, static_cast<size_t>(12) * L * 4) != cudaSuccess ||
-      cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess || cudaEventCreate(&e0) != cudaSuccess ||
-      cudaEventCreate(&e1) != cudaSuccess || cudaMemcpy(dx, x.data(), x.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess) {
-    std::fprintf(stderr, "lbrr_b200: bench buffers: %s\n", cudaGetErrorString(cudaGetLastError()));
-    rc = 1;
-  }
-  std::vector<float> ms;
-  for (int it = 0; rc == 0 && it < a.warmup + a.iters; ++it) {
-    cudaEventRecord(e0, s);
-    if (lbrr_forward_chunk(eng.e[0], dx, L, dy, s) != LBRR_OK) {
-      std::fprintf(stderr, "lbrr_b200: forward: %s\n", lbrr_last_error());
-      rc = 1;
-      break;
-    }
-    cudaEventRecord(e1, s);
-    cudaEventSynchronize(e1);
-    float t = 0;
-    cudaEventElapsedTime(&t, e0, e1);
-    if (it >= a.warmup) ms.push_back(t);
-  }
-  if (rc == 0 && lbrr_engine_sync(eng.e[0]) != LBRR_OK) {
-    std::fprintf(stderr, "lbrr_b200: %s\n", lbrr_last_error());
-    rc = 1;
-  }
-  if (rc == 0) {
-    std::sort(ms.begin(), ms.end());
-    const double med = ms[ms.size() / 2];
-    const double flop = 6069010774016.0;  // full chunk, src/benchmark.rs:105-117
-    char line[512];
-    std::snprintf(line, sizeof line,
-                  "{\"metric\": \"ms/588800-sample chunk\", \"ms_median\": %.4f, \"ms_min\": %.4f, \"iters\": %d, "
-                  "\"warmup\": %d, \"device\": %d, \"rtf\": %.6f, \"tflops\": %.1f}",
-                  med, ms.front(), a.iters, a.warmup, a.device, med / (L / 44.1), flop / med / 1e9);
-    std::printf("%s\n", line);
-    if (!a.bench_json.empty()) {
-      std::FILE* f = std::fopen(a.bench_json.c_str(), "w");
-      if (!f || std::fprintf(f, "%s\n", line) < 0 || std::fclose(f) != 0) {
-        std::fprintf(stderr, "lbrr_b200: cannot write %s\n", a.bench_json.c_str());
-        rc = 1;
-      }
-    }
-  }
-  cudaFree(dx);
-  cudaFree(dy);
-  if (e0) cudaEventDestroy(e0);
-  if (e1) cudaEventDestroy(e1);
-  if (s) cudaStreamDestroy(s);
-  return rc;
-}
-
 }  // namespace
 
 int main(int argc, char** argv) {
+  const auto t_start = std::chrono::steady_clock::now();
   Args a;
   if (int rc = parse_args(argc, argv, a)) {
     usage();
@@ -462,7 +392,27 @@ int main(int argc, char** argv) {
   }
   if (a.print_config) return print_config(a);
   if (a.check_weights) return check_weights(a);
-  if (a.bench) return bench(a);
+  if (a.bench || a.dualbench || a.kernel_regression) {
+    BenchArgs b;
+    b.model_dir = a.model_dir;
+    b.reference = a.bench_ref;
+    b.json = a.bench_json;
+    b.output = a.bench_output;
+    b.stage = a.bench_stage;
+    b.device = a.device;
+    b.warmup = a.warmup;
+    b.iters = a.iters;
+    b.dual = a.dualbench;
+    b.process_start = t_start;
+    if (a.kernel_regression) return run_kernel_regression(b);
+    ModelConfig c;
+    std::string err, why;
+    if (!load_model_config(a.model_dir, c, err) || !supported(c, why)) {
+      std::fprintf(stderr, "lbrr_b200: model: %s\n", err.empty() ? why.c_str() : err.c_str());
+      return 1;
+    }
+    return run_bench(b);
+  }
   if (a.input.empty()) {
     usage();
     return 2;
