@@ -140,7 +140,8 @@ int lbrr_forward_back(lbrr_engine* e, int64_t len, float* stems_dev, void* strea
 
 /* Copy an internal buffer of the last forward to host memory (after syncing the
  * engine stream): "spec" [2][T][1025] complex64, "c2r" (masked spectra)
- * [12][T][1025] complex64, "pcm" [12][T][2048] fp32, "x" [T*62][256] fp32,
+ * [12][T][1025] complex64, "pcm" [12][T][2048] fp32 (only after a forward
+ * through the cuFFT back end), "x" [T*62][256] fp32,
  * "xb16" [62][T][256] fp16, "hidden" [6*62][T][1024] fp16.  `bytes` must not
  * exceed the buffer's size for the current length.  Diagnostic taps like the
  * reference's --dump-trunk dumps (src/main.rs:7055-7150). */
@@ -158,7 +159,14 @@ int lbrr_engine_sync(lbrr_engine* e);
  *   defined for Hermitian input, where those parts are zero, and torch.istft
  *   (the model definition the reference's golden gate targets) drops them.  0
  *   keeps those two bins real; 1 keeps the imaginary parts exactly as the
- *   reference's GPU path computes them.
+ *   reference's GPU path computes them; the inverse transform then runs
+ *   through cuFFT, whose C2R consumes them as the reference's does.
+ * LBRR_OPT_FFT_BACKEND  0 (default) or 1.  0: the in-house FFT kernels, the
+ *   forward transform fused with framing, spectrum and band RMSNorm, the
+ *   inverse fused with windowing, overlap-add and the envelope (no "frames"
+ *   or "pcm" buffers).  1: cuFFT R2C/C2R between separate framing, band-norm
+ *   and overlap-add kernels, the reference's decomposition
+ *   (src/stft.rs:36-57, src/main.rs:7033-7040, :7154-7160).
  * LBRR_OPT_SONG_FAIL_CHUNK  -1 (default) or a chunk index.  Test hook of the
  *   song entry point: this engine's host thread fails with LBRR_ERR_STATE just
  *   before the forward of that chunk, so the abort path of lbrr_separate_song
@@ -166,6 +174,7 @@ int lbrr_engine_sync(lbrr_engine* e);
  *   without any device fault. */
 #define LBRR_OPT_DC_NYQUIST_IMAG 1
 #define LBRR_OPT_SONG_FAIL_CHUNK 2
+#define LBRR_OPT_FFT_BACKEND 3
 /* Read-only (lbrr_engine_get_option): kernels of this library launched by the
  * last chunk forward (cuFFT's own kernels not counted); a replayed CUDA graph
  * launches the same kernels. */

@@ -286,8 +286,11 @@ struct lbrr_engine {
   // the host threads that copy them (started by the first call)
   cudaEvent_t host_ev[kHostSlices] = {};
   std::unique_ptr<HostPool> host_pool;
+  float2* twiddles = nullptr;  // [2048] exp(+2 pi i k / 2048) for the in-house FFT
+  bool pcm_valid = false;      // the last back end went through cuFFT and left "pcm"
   // options (lbrr_engine_set_option)
   bool keep_dc_imag = false;     // LBRR_OPT_DC_NYQUIST_IMAG
+  int fft_backend = 0;           // LBRR_OPT_FFT_BACKEND
   int64_t song_fail_chunk = -1;  // LBRR_OPT_SONG_FAIL_CHUNK
   int64_t kernels_per_forward = 0;  // this library's launches in the last directly issued forward
   // host-side phase times of the last weight load and per-length setup (microseconds)
@@ -434,7 +437,8 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   e->warena_bytes = carve_weights(e, kLayoutBase);
   // ---- scratch arena ----
   Carver s;
-  const size_t o_win = s.take<float>(kNfft), o_fr = s.take<float>(2 * T * kNfft), o_sp = s.take<float2>(2 * T * kBins);
+  const size_t o_win = s.take<float>(kNfft), o_tw = s.take<float2>(2048), o_fr = s.take<float>(2 * T * kNfft),
+               o_sp = s.take<float2>(2 * T * kBins);
   const size_t o_xn = s.take<__half>(T * G.xn_cols), o_x = s.take<float>(M * 256), o_h = s.take<__half>(M * 256);
   const size_t o_g = s.take<float>(M * 8), o_qkv = s.take<__half>(M * 1536), o_sc = s.take<__half>(M * 512);
   const size_t o_ao = s.take<float>(M * 256), o_xb = s.take<__half>(M * 256);
@@ -466,6 +470,7 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
   e->band_d = reinterpret_cast<int*>(S + o_d);
   e->band_o2 = reinterpret_cast<int*>(S + o_o2);
   e->window = reinterpret_cast<float*>(S + o_win);
+  e->twiddles = reinterpret_cast<float2*>(S + o_tw);
   e->frames = reinterpret_cast<float*>(S + o_fr);
   e->spec = reinterpret_cast<float2*>(S + o_sp);
   e->xn = reinterpret_cast<__half*>(S + o_xn);
@@ -500,7 +505,12 @@ extern "C" int lbrr_engine_create(int device, const lbrr_model_desc* desc, int64
     dd[b] = G.d[b];
     o2[b] = G.o2[b];
   }
+  std::vector<float2> tw(2048);
+  for (int k = 0; k < 2048; ++k)
+    tw[k] = make_float2(static_cast<float>(std::cos(2.0 * M_PI * k / 2048.0)),
+                        static_cast<float>(std::sin(2.0 * M_PI * k / 2048.0)));
   ce = cudaMemcpy(e->window, win.data(), win.size() * 4, cudaMemcpyHostToDevice);
+  if (ce == cudaSuccess) ce = cudaMemcpy(e->twiddles, tw.data(), tw.size() * sizeof(float2), cudaMemcpyHostToDevice);
   if (ce == cudaSuccess) ce = cudaMemcpy(e->band_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
   if (ce == cudaSuccess) ce = cudaMemcpy(e->band_f0, f0.data(), f0.size() * 4, cudaMemcpyHostToDevice);
   if (ce == cudaSuccess) ce = cudaMemcpy(e->band_d, dd.data(), dd.size() * 4, cudaMemcpyHostToDevice);
@@ -825,8 +835,15 @@ static int setup_length_impl(lbrr_engine* e, int64_t len) {
     CK(cudaMalloc(&e->inv_env, env.size() * sizeof(float)));
     CK(cudaMemcpy(e->inv_env, env.data(), env.size() * 4, cudaMemcpyHostToDevice));
   }
-  // cuFFT plans: R2C batch 2T (src/stft.rs:36-45), C2R batch 12T
-  if (e->cur_T != T) {
+  // cuFFT plans (R2C batch 2T, src/stft.rs:36-45; C2R batch 12T), only for the
+  // cuFFT back end or the reference's DC/Nyquist semantics
+  const bool need_cufft = e->fft_backend == 1 || e->keep_dc_imag;
+  if (!need_cufft && e->plans) {
+    cufftDestroy(e->plan_r2c);
+    cufftDestroy(e->plan_c2r);
+    e->plans = false;
+  }
+  if (need_cufft && (e->cur_T != T || !e->plans)) {
     if (e->plans) {
       cufftDestroy(e->plan_r2c);
       cufftDestroy(e->plan_c2r);
@@ -864,13 +881,22 @@ static RowNorm attn_norm(lbrr_engine* e, int k) {
   return n;
 }
 
+static bool use_cufft_front(const lbrr_engine* e) { return e->fft_backend == 1; }
+static bool use_cufft_back(const lbrr_engine* e) { return e->fft_backend == 1 || e->keep_dc_imag; }
+
 static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t st) {
   const BandGeom& G = geom();
   const int T = e->cur_T;
-  CKL(stft_frames(x, e->window, e->frames, static_cast<int>(len), T, st));
-  CKFFT(cufftSetStream(e->plan_r2c, st));
-  CKFFT(cufftExecR2C(e->plan_r2c, e->frames, reinterpret_cast<cufftComplex*>(e->spec)));
-  CKL(band_norm(e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols, T, kNumBands, st));
+  if (use_cufft_front(e)) {
+    CKL(stft_frames(x, e->window, e->frames, static_cast<int>(len), T, st));
+    CKFFT(cufftSetStream(e->plan_r2c, st));
+    CKFFT(cufftExecR2C(e->plan_r2c, e->frames, reinterpret_cast<cufftComplex*>(e->spec)));
+    CKL(band_norm(e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols, T, kNumBands, st));
+  } else {
+    // framing + FFT + spectrum + band RMSNorm in one kernel
+    CKL(stft_front(x, e->window, e->twiddles, e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols,
+                   static_cast<int>(len), T, kNumBands, st));
+  }
   // band split, fused with step 0's pre-attention RMSNorm + gates
   CKL(gemm_bandsplit(e->xn, G.xn_cols, e->band_w, G.kpad_max, e->band_b, e->x, T, kNumBands, e->tiles_band,
                      e->n_band, attn_norm(e, 0), e->status, st));
@@ -909,9 +935,16 @@ static int run_back(lbrr_engine* e, int64_t len, float* out, cudaStream_t st) {
                  st));
   CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
                  G.n2tot, e->tiles_m2, e->n_m2, e->keep_dc_imag, e->status, st));
-  CKFFT(cufftSetStream(e->plan_c2r, st));
-  CKFFT(cufftExecC2R(e->plan_c2r, reinterpret_cast<cufftComplex*>(e->c2r), e->pcm));
-  CKL(istft_ola(e->pcm, e->window, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
+  if (use_cufft_back(e)) {
+    CKFFT(cufftSetStream(e->plan_c2r, st));
+    CKFFT(cufftExecC2R(e->plan_c2r, reinterpret_cast<cufftComplex*>(e->c2r), e->pcm));
+    CKL(istft_ola(e->pcm, e->window, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
+    e->pcm_valid = true;
+  } else {
+    // inverse FFT + window + overlap-add + envelope in one kernel
+    CKL(istft_back(e->c2r, e->window, e->twiddles, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
+    e->pcm_valid = false;
+  }
   return LBRR_OK;
 }
 
@@ -1034,7 +1067,12 @@ extern "C" int lbrr_engine_read_buffer(lbrr_engine* e, const char* name, void* d
   const std::string n(name);
   if (n == "spec") src = e->spec, cap = 2 * T * kBins * sizeof(float2);
   else if (n == "c2r") src = e->c2r, cap = 2 * kStems * T * kBins * sizeof(float2);
-  else if (n == "pcm") src = e->pcm, cap = 2 * kStems * T * kNfft * sizeof(float);
+  else if (n == "pcm") {
+    if (!e->pcm_valid)
+      return fail(LBRR_ERR_STATE, "no \"pcm\" frames: the in-house back end fuses the inverse FFT with the "
+                                  "overlap-add (select LBRR_OPT_FFT_BACKEND 1 to keep them)");
+    src = e->pcm, cap = 2 * kStems * T * kNfft * sizeof(float);
+  }
   else if (n == "x") src = e->x, cap = M * 256 * sizeof(float);
   else if (n == "xb16") src = e->xb16, cap = M * 256 * sizeof(__half);
   else if (n == "hidden") src = e->hidden, cap = kStems * M * 1024 * sizeof(__half);
@@ -1063,11 +1101,22 @@ extern "C" int lbrr_engine_set_option(lbrr_engine* e, int option, int64_t value)
         CK(cudaStreamSynchronize(e->stream));
         drop_graph(e);  // the captured launches carry the old setting
         e->keep_dc_imag = value == 1;
+        e->cur_len = -1;  // the next forward redoes the per-length setup (cuFFT plans on demand)
       }
       return LBRR_OK;
     case LBRR_OPT_SONG_FAIL_CHUNK:
       if (value < -1) return fail(LBRR_ERR_INVALID, "LBRR_OPT_SONG_FAIL_CHUNK takes -1 or a chunk index");
       e->song_fail_chunk = value;
+      return LBRR_OK;
+    case LBRR_OPT_FFT_BACKEND:
+      if (value != 0 && value != 1) return fail(LBRR_ERR_INVALID, "LBRR_OPT_FFT_BACKEND takes 0 or 1");
+      if (e->fft_backend != value) {
+        DeviceGuard g(e->device);
+        CK(cudaStreamSynchronize(e->stream));
+        drop_graph(e);
+        e->fft_backend = static_cast<int>(value);
+        e->cur_len = -1;  // the next forward redoes the per-length setup (cuFFT plans on demand)
+      }
       return LBRR_OK;
     default:
       return fail(LBRR_ERR_INVALID, "unknown engine option " + std::to_string(option));
@@ -1079,6 +1128,7 @@ extern "C" int lbrr_engine_get_option(const lbrr_engine* e, int option, int64_t*
   switch (option) {
     case LBRR_OPT_DC_NYQUIST_IMAG: *value = e->keep_dc_imag ? 1 : 0; return LBRR_OK;
     case LBRR_OPT_SONG_FAIL_CHUNK: *value = e->song_fail_chunk; return LBRR_OK;
+    case LBRR_OPT_FFT_BACKEND: *value = e->fft_backend; return LBRR_OK;
     case LBRR_INFO_KERNELS_PER_FORWARD: *value = e->kernels_per_forward; return LBRR_OK;
     case LBRR_INFO_WEIGHTS_READ_US: *value = e->us_read; return LBRR_OK;
     case LBRR_INFO_WEIGHTS_PARSE_US: *value = e->us_parse; return LBRR_OK;

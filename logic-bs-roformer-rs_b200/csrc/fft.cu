@@ -1,0 +1,327 @@
+// In-house FFT for the STFT front end and the ISTFT back end, fused with the
+// bandwidth work around them (replaces cuFFT R2C/C2R of the reference,
+// src/stft.rs:36-57, src/main.rs:7033-7040, :7154-7160, together with
+// frame_hann_reflect :396-429, spec_reorder :1649-1677, bandsplit_norm
+// :792-828 and istft_ola :5024-5039).
+//
+// Both transforms are 2048-point real FFTs computed as one 1024-point complex
+// FFT of z[m] = x[2m] + i x[2m+1] plus the usual split step
+//   X[k] = E[k] + W^k O[k],  E[k] = (Z[k] + conj Z[1024-k]) / 2,
+//   O[k] = (Z[k] - conj Z[1024-k]) / 2i,  W = exp(-2 pi i / 2048),
+// and its inverse.  The 1024-point FFT is 32 x 32 (four-step): one warp owns a
+// frame; lane b first runs a 32-point DFT over inputs 32a + b (a = 0..31) in
+// registers, multiplies by w^(b c), and hands the result to lane c through a
+// 33-column padded shared-memory transpose for the second 32-point DFT.  The
+// 32-point DFTs are radix-2 decimation in frequency with twiddles folded into
+// immediates; the 1024/2048-point twiddles come from a per-CTA table of
+// exp(2 pi i k / 2048) computed in double precision on the host.
+//
+//   stft_front_kernel  reflect-padded Hann framing of both channels, forward
+//                      FFT, spectrum out ([2][T][1025], needed by the mask
+//                      stage) and the band RMSNorm of every band straight from
+//                      shared memory into the fp16 band-split input xn.
+//   istft_back_kernel  one channel, a run of 512-sample output blocks: the
+//                      inverse FFT of every frame touching them (three frames
+//                      of overlap recomputed by the neighbouring CTA), Hann
+//                      window, overlap-add in frame order, division by the
+//                      window-square envelope, crop -- one pass over the
+//                      masked spectra and one write of the waveform.
+// The DC and Nyquist bins are taken as real (their imaginary parts, which a
+// real signal's spectrum does not have, are ignored), the torch.istft
+// convention.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace lbrr {
+
+namespace {
+
+constexpr int kTwN = 2048;                 // twiddle table entries: exp(2 pi i k / 2048)
+constexpr int kXpose = 32 * 33;            // padded 32 x 32 complex transpose (8448 B)
+__device__ constexpr float kW32c[16] = {1.0f,           9.807852804e-01f, 9.238795325e-01f, 8.314696123e-01f,
+                             7.071067812e-01f, 5.555702330e-01f, 3.826834324e-01f, 1.950903220e-01f,
+                             0.0f,           -1.950903220e-01f, -3.826834324e-01f, -5.555702330e-01f,
+                             -7.071067812e-01f, -8.314696123e-01f, -9.238795325e-01f, -9.807852804e-01f};
+__device__ constexpr float kW32s[16] = {0.0f,           1.950903220e-01f, 3.826834324e-01f, 5.555702330e-01f,
+                             7.071067812e-01f, 8.314696123e-01f, 9.238795325e-01f, 9.807852804e-01f,
+                             1.0f,           9.807852804e-01f, 9.238795325e-01f, 8.314696123e-01f,
+                             7.071067812e-01f, 5.555702330e-01f, 3.826834324e-01f, 1.950903220e-01f};
+
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+__device__ __forceinline__ float2 cconj(float2 a) { return make_float2(a.x, -a.y); }
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+
+__host__ __device__ constexpr int bitrev5(int i) {
+  return ((i & 1) << 4) | ((i & 2) << 2) | (i & 4) | ((i & 8) >> 2) | ((i & 16) >> 4);
+}
+
+// In-register 32-point DFT, radix-2 decimation in frequency: on return v[i]
+// holds output bitrev5(i).  INV selects exp(+2 pi i jk / 32) (inverse,
+// unnormalised) over exp(-2 pi i jk / 32).
+template <bool INV>
+__device__ __forceinline__ void dft32(float2 (&v)[32]) {
+#pragma unroll
+  for (int span = 16; span >= 1; span >>= 1) {
+#pragma unroll
+    for (int start = 0; start < 32; start += 2 * span) {
+#pragma unroll
+      for (int j = 0; j < span; ++j) {
+        const float2 a = v[start + j], b = v[start + j + span];
+        v[start + j] = cadd(a, b);
+        const float2 d = csub(a, b);
+        const int k = j * (16 / span);  // twiddle W_32^k
+        if (k == 0) {
+          v[start + j + span] = d;
+        } else if (k == 8) {
+          v[start + j + span] = INV ? make_float2(-d.y, d.x) : make_float2(d.y, -d.x);
+        } else {
+          const float2 w = make_float2(kW32c[k], INV ? kW32s[k] : -kW32s[k]);
+          v[start + j + span] = cmul(d, w);
+        }
+      }
+    }
+  }
+}
+
+// tw[k] = exp(+2 pi i k / 2048) for k in [0, 2048).
+__device__ __forceinline__ float2 twiddle(const float2* tw, int k) { return tw[k & (kTwN - 1)]; }
+
+// 1024-point complex FFT of one frame by one warp.  On entry lane b holds
+// v[a] = input[32a + b]; on return lane c holds v[i] = output[c + 32 *
+// bitrev5(i)].  `xp` is the warp's padded transpose buffer.
+template <bool INV>
+__device__ __forceinline__ void fft1024_warp(float2 (&v)[32], float2* xp, const float2* tw, int lane) {
+  dft32<INV>(v);
+  // v[i] = U[b][c], c = bitrev5(i); times w^(b c), w = exp(+-2 pi i / 1024) = tw[2 b c]
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int c = bitrev5(i);
+    float2 w = twiddle(tw, 2 * lane * c);
+    if (!INV) w.y = -w.y;
+    xp[c * 33 + lane] = c == 0 ? v[i] : cmul(v[i], w);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int b = 0; b < 32; ++b) v[b] = xp[lane * 33 + b];
+  __syncwarp();
+  dft32<INV>(v);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Front end: frames t0 .. t0+3 of both channels per CTA (8 warps: warp
+// = 2 * frame + channel), then band RMSNorm of all bands of those frames.
+// ---------------------------------------------------------------------------
+constexpr int kFrontFrames = 4;
+constexpr int kFrontThreads = 2 * kFrontFrames * 32;
+constexpr int kFrontSpec = 1028;  // per (frame, channel) spectrum slot in shared memory (1025 used)
+constexpr int kFrontSmem = (kTwN + 2 * kFrontFrames * (kXpose + kFrontSpec)) * 8;
+
+__global__ void __launch_bounds__(kFrontThreads) stft_front_kernel(const float* __restrict__ x,
+                                                                   const float* __restrict__ win,
+                                                                   const float2* __restrict__ twg,
+                                                                   float2* __restrict__ spec,
+                                                                   const float* __restrict__ gamma,
+                                                                   const int* __restrict__ tab, __half* __restrict__ xn,
+                                                                   int xn_cols, int len, int T, int nb) {
+  extern __shared__ __align__(16) float2 fsm[];
+  float2* tw = fsm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kTwN; i += blockDim.x) tw[i] = twg[i];
+  __syncthreads();
+  const int fl = warp >> 1, ch = warp & 1;
+  const int t = blockIdx.x * kFrontFrames + fl;
+  float2* xp = fsm + kTwN + warp * kXpose;
+  float2* xs = fsm + kTwN + 2 * kFrontFrames * kXpose + warp * kFrontSpec;
+  if (t < T) {
+    // z[m] = x[2m] + i x[2m+1] of the windowed, reflect-padded frame; lane b loads z[32a + b]
+    float2 v[32];
+    const int pad = kNfft / 2;
+#pragma unroll
+    for (int a = 0; a < 32; ++a) {
+      const int j = 64 * a + 2 * lane;
+      float s2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int g = t * kHop + j + e;
+        const int src = g < pad ? pad - g : (g >= len + pad ? 2 * len + pad - 2 - g : g - pad);
+        s2[e] = __ldg(x + 2ll * src + ch) * __ldg(win + j + e);
+      }
+      v[a] = make_float2(s2[0], s2[1]);
+    }
+    fft1024_warp<false>(v, xp, tw, lane);
+    // Z[c + 32 d] (d = bitrev5(i)) into the transpose buffer, linear order
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) xp[lane + 32 * bitrev5(i)] = v[i];
+    __syncwarp();
+    // split step: X[k] for k = lane + 32 j, and X[1024]
+    float2* out = spec + (static_cast<size_t>(ch) * T + t) * kBins;
+#pragma unroll 4
+    for (int j = 0; j < 32; ++j) {
+      const int k = lane + 32 * j;
+      const float2 z = xp[k], zc = cconj(xp[(kBins - 1 - k) & 1023]);
+      const float2 e = make_float2(0.5f * (z.x + zc.x), 0.5f * (z.y + zc.y));
+      const float2 d = make_float2(0.5f * (z.x - zc.x), 0.5f * (z.y - zc.y));
+      const float2 o = make_float2(d.y, -d.x);  // d / i
+      const float2 w = cconj(twiddle(tw, k));   // exp(-2 pi i k / 2048)
+      const float2 X = cadd(e, cmul(o, w));
+      xs[k] = X;
+      out[k] = X;
+    }
+    if (lane == 0) {
+      const float2 z0 = xp[0];
+      const float2 X = make_float2(z0.x - z0.y, 0.f);  // E[0] - O[0]
+      xs[1024] = X;
+      out[1024] = X;
+    }
+  }
+  __syncthreads();
+  // band RMSNorm: one warp per (frame, band) of this CTA (bandsplit_norm:
+  // v * sqrt(d_b) / max(|v|, 1e-12) * gamma, zero-padded to the band's slot)
+  for (int task = warp; task < kFrontFrames * nb; task += 2 * kFrontFrames) {
+    const int f = task / nb, b = task - f * nb;
+    const int tt = blockIdx.x * kFrontFrames + f;
+    if (tt >= T) continue;
+    const int d = tab[b * 8 + 0], f0 = tab[b * 8 + 1], koff = tab[b * 8 + 2], kpad = tab[b * 8 + 3],
+              goff = tab[b * 8 + 4];
+    const float2* s0 = fsm + kTwN + 2 * kFrontFrames * kXpose + (2 * f) * kFrontSpec;
+    float vals[17];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 17; ++i) {
+      const int j = lane + 32 * i;
+      float vv = 0.f;
+      if (j < d) {
+        const float2 s = s0[((j >> 1) & 1) * kFrontSpec + f0 + (j >> 2)];
+        vv = (j & 1) ? s.y : s.x;
+      }
+      vals[i] = vv;
+      ss += vv * vv;
+    }
+    ss = warp_sum(ss);
+    const float scale = sqrtf(static_cast<float>(d)) / fmaxf(sqrtf(ss), 1e-12f);
+    __half* row = xn + static_cast<long long>(tt) * xn_cols + koff;
+#pragma unroll
+    for (int i = 0; i < 17; ++i) {
+      const int j = lane + 32 * i;
+      if (j < kpad) {
+        const float vv = j < d ? __fmul_rn(__fmul_rn(vals[i], scale), __ldg(gamma + goff + j)) : 0.f;
+        row[j] = __float2half_rn(vv);
+      }
+    }
+    for (int j = lane + 32 * 17; j < kpad; j += 32) row[j] = __float2half_rn(0.f);
+  }
+}
+
+cudaError_t stft_front(const float* x, const float* window, const float2* twiddles, float2* spec, const float* gamma,
+                       const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb, cudaStream_t st) {
+  static unsigned long long configured = 0;
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(stft_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFrontSmem);
+  });
+  if (e != cudaSuccess) return e;
+  count_launch();
+  stft_front_kernel<<<(T + kFrontFrames - 1) / kFrontFrames, kFrontThreads, kFrontSmem, st>>>(
+      x, window, twiddles, spec, gamma, band_tab, xn, xn_cols, len, T, nb);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Back end: channel sc = blockIdx.y, output blocks [k0, k0 + kBackBlocks) of
+// 512 padded samples, k0 = 2 + blockIdx.x * kBackBlocks.  Frames k0-3 ..
+// k0+kBackBlocks-1 (16; two per warp) are inverse-transformed into shared
+// memory (x[n] * w[n], already divided by 2048), then every output sample sums
+// its (up to four) frames in frame order and takes the envelope.
+// ---------------------------------------------------------------------------
+constexpr int kBackWarps = 8;
+constexpr int kBackFramesPerCta = 2 * kBackWarps;
+constexpr int kBackBlocks = kBackFramesPerCta - 3;
+constexpr int kBackSlot = kXpose;  // a frame's 2048 floats live in its (larger) transpose slot
+constexpr int kBackSmem = (kTwN + kBackFramesPerCta * kBackSlot) * 8;
+
+__global__ void __launch_bounds__(kBackWarps * 32) istft_back_kernel(const float2* __restrict__ c2r,
+                                                                     const float* __restrict__ win,
+                                                                     const float2* __restrict__ twg,
+                                                                     const float* __restrict__ inv_env,
+                                                                     float* __restrict__ out, int len, int T) {
+  extern __shared__ __align__(16) float2 bsm[];
+  float2* tw = bsm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sc = blockIdx.y;
+  const int k0 = 2 + blockIdx.x * kBackBlocks;
+  for (int i = threadIdx.x; i < kTwN; i += blockDim.x) tw[i] = twg[i];
+  __syncthreads();
+#pragma unroll 1
+  for (int r = 0; r < 2; ++r) {
+    const int slot = warp + r * kBackWarps;
+    const int t = k0 - 3 + slot;
+    if (t < 0 || t >= T) continue;
+    float2* xp = bsm + kTwN + slot * kBackSlot;
+    const float2* X = c2r + (static_cast<size_t>(sc) * T + t) * kBins;
+    // Z'[k] = (X[k] + conj X[1024-k]) + i (X[k] - conj X[1024-k]) exp(+2 pi i k / 2048),
+    // DC and Nyquist taken as real; lane b builds Z'[32a + b]
+    float2 v[32];
+#pragma unroll
+    for (int a = 0; a < 32; ++a) {
+      const int k = 32 * a + lane;
+      float2 xk = __ldg(X + k), xr = __ldg(X + 1024 - k);
+      if (k == 0) {
+        xk.y = 0.f;
+        xr.y = 0.f;
+      }
+      const float2 xc = cconj(xr);
+      const float2 e = cadd(xk, xc);
+      const float2 o = cmul(csub(xk, xc), twiddle(tw, k));
+      v[a] = make_float2(e.x - o.y, e.y + o.x);  // e + i o
+    }
+    fft1024_warp<true>(v, xp, tw, lane);
+    // y[c + 32 d] = 2048 (x[2m] + i x[2m+1]), m = c + 32 d: windowed samples into the slot
+    __syncwarp();
+    float* fr = reinterpret_cast<float*>(xp);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int m = lane + 32 * bitrev5(i);
+      const float2 w2 = __ldg(reinterpret_cast<const float2*>(win) + m);
+      fr[2 * m] = (v[i].x * (1.0f / 2048.0f)) * w2.x;
+      fr[2 * m + 1] = (v[i].y * (1.0f / 2048.0f)) * w2.y;
+    }
+  }
+  __syncthreads();
+  // overlap-add in frame order, envelope, crop to [n_fft/2, n_fft/2 + len)
+  const int p_lo = max(k0 * kHop, kNfft / 2), p_hi = min((k0 + kBackBlocks) * kHop, kNfft / 2 + len);
+  float* o = out + static_cast<size_t>(sc) * len;
+  for (int p = p_lo + threadIdx.x; p < p_hi; p += blockDim.x) {
+    const int k = p / kHop;
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 3; q >= 0; --q) {
+      const int t = k - q;
+      if (t < 0 || t >= T) continue;
+      const float* fr = reinterpret_cast<const float*>(bsm + kTwN + (t - (k0 - 3)) * kBackSlot);
+      sum += fr[p - t * kHop];
+    }
+    o[p - kNfft / 2] = sum * __ldg(inv_env + p);
+  }
+}
+
+cudaError_t istft_back(const float2* c2r, const float* window, const float2* twiddles, const float* inv_env,
+                       float* out, int len, int T, int channels, cudaStream_t st) {
+  static unsigned long long configured = 0;
+  cudaError_t e = once_per_device(configured, [] {
+    return cudaFuncSetAttribute(istft_back_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBackSmem);
+  });
+  if (e != cudaSuccess) return e;
+  const int k_last = (len + kNfft / 2 - 1) / kHop;  // last output block
+  const int groups = (k_last - 2 + 1 + kBackBlocks - 1) / kBackBlocks;
+  count_launch();
+  istft_back_kernel<<<dim3(groups, channels), kBackWarps * 32, kBackSmem, st>>>(c2r, window, twiddles, inv_env, out,
+                                                                                 len, T);
+  return cudaGetLastError();
+}
+
+}  // namespace lbrr

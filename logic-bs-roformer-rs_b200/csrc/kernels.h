@@ -94,6 +94,14 @@ cudaError_t norm_gates(const float* x, const float* gamma, const float* gate_w, 
 cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_env, float* out, int len, int T,
                       int channels, cudaStream_t st);
 
+// ---- in-house FFT, fused with its neighbours (fft.cu) ------------------------
+// twiddles: [2048] exp(+2 pi i k / 2048) as float2
+cudaError_t stft_front(const float* x_interleaved, const float* window, const float2* twiddles, float2* spec,
+                       const float* gamma, const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb,
+                       cudaStream_t st);
+cudaError_t istft_back(const float2* c2r, const float* window, const float2* twiddles, const float* inv_env,
+                       float* out, int len, int T, int channels, cudaStream_t st);
+
 // cudaFuncSetAttribute (the dynamic shared-memory opt-in) acts on the current
 // device only.  Runs `setup` once per device (devices 0..63, bit d of `done`)
 // before the first launch there; a failed setup is retried on the next call.

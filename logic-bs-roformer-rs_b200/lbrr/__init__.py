@@ -132,6 +132,7 @@ def _ptr(t):
 # engine options (include/lbrr_gpu.h)
 OPT_DC_NYQUIST_IMAG = 1
 OPT_SONG_FAIL_CHUNK = 2
+OPT_FFT_BACKEND = 3
 INFO_KERNELS_PER_FORWARD = 100
 
 CUDA_STREAM_LEGACY = 0x1  # cudaStreamLegacy: the legacy default stream named explicitly

@@ -96,7 +96,7 @@ def test_bench_json(setup, tmp_path):
                             "sample_rate": 44100}
     assert rep["identity"]["model_sha256"] and len(rep["identity"]["source_sha256"]) == 64
     assert rep["identity"]["fixture_id"] == "golden"
-    assert rep["ola_vs_host"]["finite"] and rep["ola_vs_host"]["max_abs_error"] <= 1e-6
+    assert rep["ola_vs_host"]["finite"] and rep["ola_vs_host"]["max_abs_error"] <= 2e-6 * max(1.0, np.abs(ref).max())
     assert rep["mfu"]["matrix_flops"] == R.matrix_flops(259)  # the FLOP count follows the input length
     assert rep["memory_bytes"]["weights"] > 300e6
     c = rep["correctness"]

@@ -178,20 +178,53 @@ def identity_mask_weights(seed=5):
     return w
 
 
+@pytest.mark.parametrize("backend", [0, 1], ids=["inhouse_fft", "cufft"])
 @pytest.mark.parametrize("length", [1025, 18944, 132300, 588800])
-def test_ola_impulses_identity_mask(engine, length):
+def test_ola_impulses_identity_mask(engine, length, backend):
     """ola_regression (src/main.rs:7943-7965): impulses at both ends of both
     channels come back on every stem to 1e-6; silence stays silent; every
-    output slot is written (the output starts as NaN)."""
+    output slot is written (the output starts as NaN) -- through the in-house
+    fused FFT kernels and through the cuFFT back end."""
+    import lbrr
     engine.upload_weights(identity_mask_weights())
-    for silent in (False, True):
-        x = np.zeros((2, length), np.float32)
-        if not silent:
-            x[0, 0], x[0, length - 1], x[1, 31], x[1, length - 1] = 0.5, 1.0, -0.25, 0.125
-        got = _forward(engine, x)
-        assert np.isfinite(got).all()
-        err = np.abs(got - x[None]).max()
-        assert err <= 1e-6, (length, silent, err)
+    engine.set_option(lbrr.OPT_FFT_BACKEND, backend)
+    try:
+        for silent in (False, True):
+            x = np.zeros((2, length), np.float32)
+            if not silent:
+                x[0, 0], x[0, length - 1], x[1, 31], x[1, length - 1] = 0.5, 1.0, -0.25, 0.125
+            got = _forward(engine, x)
+            assert np.isfinite(got).all()
+            err = np.abs(got - x[None]).max()
+            assert err <= 1e-6, (length, silent, err)
+    finally:
+        engine.set_option(lbrr.OPT_FFT_BACKEND, 0)
+
+
+def test_inhouse_fft_matches_cufft_and_oracle(engine):
+    """The fused in-house front end gives the oracle's spectrum (torch.fft in
+    double) to fp32 accuracy, as cuFFT does; the whole forward through either
+    FFT back end meets the 60 dB bar against the oracle, and the two agree."""
+    import lbrr
+    w = R.make_weights(seed=2, gamma_noise=0.1)
+    engine.upload_weights(w)
+    audio = R.synth_audio(SHORT, seed=13)
+    T = R.num_frames(SHORT)
+    ref_spec = R.stft(torch.from_numpy(audio)).numpy()
+    outs, specs = {}, {}
+    for backend in (0, 1):
+        engine.set_option(lbrr.OPT_FFT_BACKEND, backend)
+        outs[backend] = _forward(engine, audio)
+        specs[backend] = engine.read_buffer("spec", (2, T, 1025), np.complex64)
+    engine.set_option(lbrr.OPT_FFT_BACKEND, 0)
+    for backend in (0, 1):
+        e = rel_err(specs[backend].view(np.float32), ref_spec.view(np.float32))
+        assert e < 2e-6, (backend, e)
+    ref = R.Oracle(w, "f16path").forward(torch.from_numpy(audio)).numpy()
+    for backend in (0, 1):
+        worst = min(snr_db(outs[backend][s], ref[s]) for s in range(6))
+        assert worst >= 60.0, (backend, worst)
+    assert min(snr_db(outs[0][s], outs[1][s]) for s in range(6)) >= 60.0
 
 
 # ---------------------------------------------------------------------------
