@@ -211,11 +211,12 @@ class Engine:
         length = x_dev.numel() // 2
         check(lib().lbrr_forward_chunk(self.handle, _ptr(x_dev), length, _ptr(out_dev), _stream(stream)))
 
-    def forward_host(self, x_host: np.ndarray) -> np.ndarray:
-        """End to end from host memory: x [len][2] fp32 -> stems [6][2][len] fp32."""
+    def forward_host(self, x_host: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        """End to end from host memory: x [len][2] fp32 -> stems [6][2][len] fp32
+        (written into `out` when given: a C-contiguous fp32 array of that shape)."""
         x = np.ascontiguousarray(x_host, dtype=np.float32)
         length = x.shape[0]
-        out = np.empty((STEMS, 2, length), dtype=np.float32)
+        out = _out_array(out, (STEMS, 2, length))
         check(lib().lbrr_forward_chunk_host(self.handle, x.ctypes.data, length, out.ctypes.data))
         return out
 
@@ -266,12 +267,28 @@ class Engine:
             pass
 
 
-def separate(engines, audio_planar: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER) -> np.ndarray:
+def _out_array(out, shape):
+    if out is None:
+        return np.empty(shape, dtype=np.float32)
+    if out.shape != shape or out.dtype != np.float32 or not out.flags["C_CONTIGUOUS"]:
+        raise LbrrError(ERR_INVALID, f"out must be a C-contiguous float32 array of shape {shape}")
+    return out
+
+
+def separate(engines, audio: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER, interleaved=False,
+             out: np.ndarray | None = None) -> np.ndarray:
     """Whole-song demix over one or more engines (separate(), src/main.rs:7598-7819).
-    audio_planar: [2][len] fp32 -> stems [6][2][len] fp32."""
-    x = np.ascontiguousarray(np.asarray(audio_planar, dtype=np.float32).T)
+    audio: planar [2][len] fp32, or interleaved [len][2] (the WAV layout the C
+    ABI takes, passed without a copy) with interleaved=True -> stems
+    [6][2][len] fp32, written into `out` when given."""
+    if interleaved:
+        x = np.ascontiguousarray(audio, dtype=np.float32)
+        if x.ndim != 2 or x.shape[1] != 2:
+            raise LbrrError(ERR_INVALID, "interleaved audio must have shape [len][2]")
+    else:
+        x = np.ascontiguousarray(np.asarray(audio, dtype=np.float32).T)
     length = x.shape[0]
-    out = np.empty((STEMS, 2, length), dtype=np.float32)
+    out = _out_array(out, (STEMS, 2, length))
     hs = (C.c_void_p * len(engines))(*[e.handle for e in engines])
     plan = ChunkPlan(chunk, step, border)
     check(lib().lbrr_separate_song(hs, len(engines), x.ctypes.data, length, C.byref(plan), out.ctypes.data))
