@@ -431,8 +431,16 @@ def run_song(torch, lbrr, eng, rank, world, dist, cpu_group=None):
         dt = time.perf_counter() - t0
         for e in engines[1:]:
             e.close()
+        # BASELINE config 4 as written: 50 % overlap, Hann-weighted overlap-add (28 chunks)
+        lbrr.separate(engines, audio_il, interleaved=True, out=stems, **lbrr.HANN50)  # warm
+        t0 = time.perf_counter()
+        lbrr.separate(engines, audio_il, interleaved=True, out=stems, **lbrr.HANN50)
+        dt_h = time.perf_counter() - t0
         result = {"seconds": round(dt, 4), "rtf": round(dt / (SONG_LEN / SR), 6), **info,
-                  "host_buffers": "interleaved input and the [6][2][len] output array allocated before the timed call"}
+                  "host_buffers": "interleaved input and the [6][2][len] output array allocated before the timed call",
+                  "hann50": {"seconds": round(dt_h, 4), "rtf": round(dt_h / (SONG_LEN / SR), 6),
+                             "chunks": len(song.chunk_starts(SONG_LEN, 588800, 294400, 294400)),
+                             "plan": "chunk 588800 / step 294400 / border 294400, Hann fade (BASELINE config 4)"}}
     if dist:
         dist.barrier(group=cpu_group)
     return result

@@ -66,18 +66,27 @@ typedef struct lbrr_weight_view {
   int64_t numel;
 } lbrr_weight_view;
 
-/* Song chunking (src/main.rs:7617-7619): chunk 588800, step 559360, border 29440. */
+/* Song chunking.  The reference plan (src/main.rs:7617-7619, tools/bench_ref.py:
+ * 13, :47-65): chunk 588800, step 559360, border 29440, linear fade of width
+ * border.  BASELINE config 4's plan: chunk 588800, step 294400 (50 % overlap),
+ * border 294400, Hann fade.  Either way the song is reflect-padded by `border`
+ * on the left, each chunk's output y is accumulated as y * w with w * w into a
+ * counter (the first chunk's leading and the last chunk's trailing `border`
+ * samples weighted 1), and the sum is divided by max(counter, 1e-8). */
+#define LBRR_FADE_LINEAR 0  /* w = ramps of width border at both chunk ends */
+#define LBRR_FADE_HANN 1    /* w = periodic Hann window over the whole chunk */
 typedef struct lbrr_chunk_plan {
   int64_t chunk;
   int64_t step;
   int64_t border;
+  int64_t fade;   /* LBRR_FADE_LINEAR (0, a zero-initialised plan) or LBRR_FADE_HANN */
 } lbrr_chunk_plan;
 
 /* Last error message of the calling thread (replaces wrap_last_error,
  * tools/cudnn_sdpa_wrap.cpp:68, :244).  Never NULL. */
 const char* lbrr_last_error(void);
 
-/* ABI version: 1. */
+/* ABI version: 2 (2 added lbrr_chunk_plan.fade, engine options and stage entry points). */
 int lbrr_abi_version(void);
 
 /* Fill `desc` with the supported model (assets/logic_bs_roformer.yaml:11-84).

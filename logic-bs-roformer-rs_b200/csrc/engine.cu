@@ -271,6 +271,8 @@ struct lbrr_engine {
   cudaEvent_t song_ev_reg[2] = {nullptr, nullptr};
   float* song_strip_out = nullptr;
   float* song_strip_in = nullptr;
+  float* song_hann = nullptr;      // Hann fade table of the last Hann plan (song_hann_len samples)
+  int64_t song_hann_len = 0;
   size_t song_strip_in_bytes = 0;
   cudaEvent_t song_ev_in[2] = {nullptr, nullptr};
   cudaEvent_t song_ev_out[2] = {nullptr, nullptr};
@@ -339,7 +341,7 @@ extern "C" const char* lbrr_last_error(void) { return g_err.c_str(); }
 // Lets the host-only translation units (safetensors.cpp) report errors through
 // the same thread-local message.
 extern "C" int lbrr_set_error_for_host(int code, const char* msg) { return fail(code, msg ? msg : ""); }
-extern "C" int lbrr_abi_version(void) { return 1; }
+extern "C" int lbrr_abi_version(void) { return 2; }
 
 extern "C" int lbrr_default_model(lbrr_model_desc* d, int32_t* freqs_out, int32_t capacity) {
   if (!d || !freqs_out || capacity < kNumBands) return fail(LBRR_ERR_INVALID, "lbrr_default_model: need 62 slots");
@@ -546,6 +548,7 @@ extern "C" void lbrr_engine_destroy(lbrr_engine* e) {
   if (e->song_copy) cudaStreamDestroy(e->song_copy);
   cudaFree(e->song_strip_out);
   cudaFree(e->song_strip_in);
+  cudaFree(e->song_hann);
   if (e->graph) cudaGraphExecDestroy(e->graph);
   for (auto& ev : e->host_ev)
     if (ev) cudaEventDestroy(ev);
@@ -1231,13 +1234,18 @@ extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t 
 // ---------------------------------------------------------------------------
 __global__ void ola_accumulate_kernel(const float* __restrict__ y, float* __restrict__ result,
                                       float* __restrict__ counter, long long out_len, long long s, int take, int c,
-                                      int border, int is_first, int is_last, int chunk_stride, int channels) {
+                                      int border, int is_first, int is_last, int chunk_stride, int channels,
+                                      const float* __restrict__ hann) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= take) return;
   float wf = 1.0f;
-  if (j < border) wf = static_cast<float>(j) / static_cast<float>(border);
-  const int j2 = c - 1 - j;
-  if (j2 < border) wf = static_cast<float>(j2) / static_cast<float>(border);
+  if (hann) {
+    wf = hann[j];
+  } else {
+    if (j < border) wf = static_cast<float>(j) / static_cast<float>(border);
+    const int j2 = c - 1 - j;
+    if (j2 < border) wf = static_cast<float>(j2) / static_cast<float>(border);
+  }
   if (is_first && j < border) wf = 1.0f;
   if (is_last && j + border >= c) wf = 1.0f;
   counter[s + j] += wf * wf;
@@ -1262,6 +1270,11 @@ std::vector<int64_t> chunk_starts(int64_t len, int64_t chunk, int64_t step, int6
   for (int64_t i = 0; i <= last; ++i) v.push_back(i * step);
   return v;
 }
+}  // namespace
+
+namespace {
+std::vector<float> hann_window_host(int64_t C);
+int ensure_song_hann(lbrr_engine* e, const std::vector<float>& w);
 }  // namespace
 
 // Plans whose chunks overlap by more than half (a sample in three or more
@@ -1289,6 +1302,10 @@ static int separate_song_serial(lbrr_engine* const* engines, int n, const float*
   }
   lbrr_engine* e0 = engines[0];
   const int channels = 2 * kStems;
+  if (P.fade == LBRR_FADE_HANN) {
+    DeviceGuard g(e0->device);
+    if (int rc = ensure_song_hann(e0, hann_window_host(P.chunk))) return rc;
+  }
   const size_t ybytes = static_cast<size_t>(channels) * C * sizeof(float);
   float *result = nullptr, *counter = nullptr, *stage = nullptr, *fin = nullptr;
   std::vector<cudaEvent_t> ev_done(n, nullptr), ev_used(n, nullptr);
@@ -1361,7 +1378,7 @@ static int separate_song_serial(lbrr_engine* const* engines, int n, const float*
       const int take = static_cast<int>(std::min<int64_t>(C, needed - s));
       ola_accumulate_kernel<<<(take + 255) / 256, 256, 0, e0->stream>>>(
           y, result, counter, needed, s, take, static_cast<int>(C), static_cast<int>(P.border), ci == 0,
-          ci + 1 == starts.size(), static_cast<int>(C), channels);
+          ci + 1 == starts.size(), static_cast<int>(C), channels, P.fade == LBRR_FADE_HANN ? e0->song_hann : nullptr);
       if (cudaGetLastError() != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "ola accumulate launch"); break; }
       if (cudaEventRecord(ev_used[slot], e0->stream) != cudaSuccess) { rc = fail(LBRR_ERR_CUDA, "event record"); break; }
     }
@@ -1429,13 +1446,28 @@ namespace {
 struct SongGeom {
   int64_t C, step, border, ov, len;
   int nc;
-  __host__ __device__ float fade(int64_t rel, int c) const {
+  const float* hann = nullptr;  // LBRR_FADE_HANN: [C] periodic Hann window on this engine's device
+  __device__ float fade(int64_t rel, int c) const {
+    if (hann) {
+      // Hann-weighted chunks; the first chunk keeps its leading border, the last its trailing border
+      if ((rel < border && c == 0) || (rel >= C - border && c == nc - 1)) return 1.0f;
+      return hann[rel];
+    }
     // linear fade of width border; the first chunk keeps its leading edge, the last its trailing edge
     if (rel < border && c != 0) return static_cast<float>(rel) / static_cast<float>(border);
     if (rel >= C - border && c != nc - 1) return static_cast<float>(C - 1 - rel) / static_cast<float>(border);
     return 1.0f;
   }
 };
+
+// Periodic Hann window of the chunk length, computed in double and rounded to
+// fp32 (the song plan of BASELINE config 4).
+std::vector<float> hann_window_host(int64_t C) {
+  std::vector<float> w(static_cast<size_t>(C));
+  for (int64_t i = 0; i < C; ++i)
+    w[i] = static_cast<float>(0.5 * (1.0 - std::cos(2.0 * M_PI * static_cast<double>(i) / static_cast<double>(C))));
+  return w;
+}
 
 // Overlap strip of chunk c: relative samples [step, C): 12 channels of y*w, then w*w.
 __global__ void song_strip_kernel(const float* __restrict__ y, float* __restrict__ strip, SongGeom g, int c) {
@@ -1476,6 +1508,19 @@ struct SongRun {
   std::vector<std::string> msg;
 };
 
+// The Hann fade table on engine e's device (current device), uploaded once per chunk length.
+int ensure_song_hann(lbrr_engine* e, const std::vector<float>& w) {
+  const int64_t C = static_cast<int64_t>(w.size());
+  if (e->song_hann && e->song_hann_len == C) return LBRR_OK;
+  cudaFree(e->song_hann);
+  e->song_hann = nullptr;
+  e->song_hann_len = 0;
+  CK(cudaMalloc(&e->song_hann, w.size() * sizeof(float)));
+  CK(cudaMemcpy(e->song_hann, w.data(), w.size() * sizeof(float), cudaMemcpyHostToDevice));
+  e->song_hann_len = C;
+  return LBRR_OK;
+}
+
 int ensure_song_buffers(lbrr_engine* e, const SongGeom& g) {
   const size_t in_b = static_cast<size_t>(g.C) * 2 * sizeof(float);
   const size_t out_b = static_cast<size_t>(g.C) * 2 * kStems * sizeof(float);
@@ -1509,10 +1554,11 @@ int ensure_song_buffers(lbrr_engine* e, const SongGeom& g) {
   return LBRR_OK;
 }
 
-void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, float* outh, const SongGeom g,
+void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, float* outh, SongGeom g,
                  const std::vector<int64_t>& starts, SongRun& run) {
   lbrr_engine* e = engines[me];
   DeviceGuard dg(e->device);
+  if (g.hann) g.hann = e->song_hann;  // this engine's copy of the fade table
   const size_t strip_b = static_cast<size_t>(2 * kStems + 1) * g.ov * sizeof(float);
   auto bail = [&](int rc) {
     run.rc[me] = rc;
@@ -1633,9 +1679,13 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
                                   const lbrr_chunk_plan* plan, float* outh) {
   if (!engines || n <= 0 || !xh || !outh) return fail(LBRR_ERR_INVALID, "NULL argument");
   if (len <= 0) return fail(LBRR_ERR_INVALID, "empty audio is unsupported");
-  const lbrr_chunk_plan P = plan ? *plan : lbrr_chunk_plan{588800, 559360, 29440};
+  const lbrr_chunk_plan P = plan ? *plan : lbrr_chunk_plan{588800, 559360, 29440, LBRR_FADE_LINEAR};
   if (P.chunk <= kNfft / 2 || P.step <= 0 || P.step > P.chunk || P.border < 0 || 2 * P.border > P.chunk)
     return fail(LBRR_ERR_INVALID, "invalid chunk plan");
+  if (P.fade != LBRR_FADE_LINEAR && P.fade != LBRR_FADE_HANN)
+    return fail(LBRR_ERR_INVALID, "chunk plan fade must be LBRR_FADE_LINEAR or LBRR_FADE_HANN");
+  if (P.fade == LBRR_FADE_LINEAR && P.border == 0 && P.step < P.chunk)
+    return fail(LBRR_ERR_INVALID, "a linear fade needs border > 0 when chunks overlap");
   for (int i = 0; i < n; ++i) {
     if (!engines[i]) return fail(LBRR_ERR_INVALID, "NULL engine");
     if (!engines[i]->weights_loaded) return fail(LBRR_ERR_STATE, "weights not loaded");
@@ -1653,6 +1703,14 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
   g.len = len;
   g.nc = static_cast<int>(starts.size());
   const int workers = std::min<int>(n, g.nc);
+  if (P.fade == LBRR_FADE_HANN) {
+    const std::vector<float> w = hann_window_host(P.chunk);
+    for (int i = 0; i < workers; ++i) {
+      DeviceGuard dg(engines[i]->device);
+      if (int rc = ensure_song_hann(engines[i], w)) return rc;
+    }
+    g.hann = engines[0]->song_hann;  // non-null marks the Hann plan; each worker uses its own copy
+  }
   SongRun run;
   run.strip_ready.assign(g.nc, 0);
   run.strip_ev.assign(g.nc, nullptr);

@@ -341,7 +341,7 @@ int separate(const Args& a) {
   if (int rc = open_engines(a, a.gpus, eng)) return rc;
   std::vector<float> out(static_cast<size_t>(2 * c.num_stems) * len);
   const auto g0 = std::chrono::steady_clock::now();
-  lbrr_chunk_plan plan{588800, 559360, 29440};
+  lbrr_chunk_plan plan{588800, 559360, 29440, LBRR_FADE_LINEAR};
   if (lbrr_separate_song(eng.e.data(), static_cast<int>(eng.e.size()), w.samples.data(), len, &plan, out.data()) !=
       LBRR_OK) {
     std::fprintf(stderr, "lbrr_b200: separation: %s\n", lbrr_last_error());

@@ -47,8 +47,13 @@ class WeightView(C.Structure):
     _fields_ = [("name", C.c_char_p), ("data", C.POINTER(C.c_float)), ("numel", C.c_int64)]
 
 
+FADE_LINEAR, FADE_HANN = 0, 1
+# BASELINE config 4's plan: 50 % overlap, Hann-weighted (28 chunks for 180.48 s)
+HANN50 = dict(chunk=588800, step=294400, border=294400, fade="hann")
+
+
 class ChunkPlan(C.Structure):
-    _fields_ = [("chunk", C.c_int64), ("step", C.c_int64), ("border", C.c_int64)]
+    _fields_ = [("chunk", C.c_int64), ("step", C.c_int64), ("border", C.c_int64), ("fade", C.c_int64)]
 
 
 _lib = None
@@ -276,7 +281,7 @@ def _out_array(out, shape):
 
 
 def separate(engines, audio: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER, interleaved=False,
-             out: np.ndarray | None = None) -> np.ndarray:
+             out: np.ndarray | None = None, fade: str = "linear") -> np.ndarray:
     """Whole-song demix over one or more engines (separate(), src/main.rs:7598-7819).
     audio: planar [2][len] fp32, or interleaved [len][2] (the WAV layout the C
     ABI takes, passed without a copy) with interleaved=True -> stems
@@ -290,7 +295,9 @@ def separate(engines, audio: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER, 
     length = x.shape[0]
     out = _out_array(out, (STEMS, 2, length))
     hs = (C.c_void_p * len(engines))(*[e.handle for e in engines])
-    plan = ChunkPlan(chunk, step, border)
+    if fade not in ("linear", "hann"):
+        raise LbrrError(ERR_INVALID, "fade must be 'linear' or 'hann'")
+    plan = ChunkPlan(chunk, step, border, FADE_HANN if fade == "hann" else FADE_LINEAR)
     check(lib().lbrr_separate_song(hs, len(engines), x.ctypes.data, length, C.byref(plan), out.ctypes.data))
     return out
 

@@ -488,18 +488,28 @@ def fade_window(chunk: int = CHUNK, border: int = BORDER) -> np.ndarray:
     return fade
 
 
-def demix(model, x: np.ndarray, chunk: int = CHUNK, step: int = STEP, border: int = BORDER) -> np.ndarray:
+def hann_fade(chunk: int) -> np.ndarray:
+    """Periodic Hann window over the chunk, in f64 rounded to f32: the weight of
+    BASELINE config 4's 50 %-overlap plan (not a reference plan; the reference
+    only has the linear fade)."""
+    n = np.arange(chunk, dtype=np.float64)
+    return (0.5 * (1.0 - np.cos(2.0 * np.pi * n / chunk))).astype(np.float32)
+
+
+def demix(model, x: np.ndarray, chunk: int = CHUNK, step: int = STEP, border: int = BORDER,
+          fade_kind: str = "linear") -> np.ndarray:
     """Chunked overlap-add demix: model(xp[..., s:s+chunk]) -> [6][2][chunk].
 
     Fade-weighted accumulate with first/last border overrides, divide by the
     accumulated fade energy, crop the border (tools/bench_ref.py:47-65).
+    fade_kind "hann" replaces the linear fade by hann_fade (same accumulation).
     x: planar [2][L].  Returns [6][2][L] fp32.
     """
     length = x.shape[-1]
     starts = chunk_starts(length, chunk, step, border)
     needed = border + length
     xp = reflect_pad(x, border, starts[-1] + chunk - needed)
-    fade = fade_window(chunk, border)
+    fade = fade_window(chunk, border) if fade_kind == "linear" else hann_fade(chunk)
     result = None
     counter = np.zeros(needed, dtype=np.float32)
     for i, s in enumerate(starts):

@@ -25,7 +25,7 @@ def test_library_exports_every_header_symbol():
 
 def test_abi_version_and_default_model():
     import lbrr
-    assert lbrr.lib().lbrr_abi_version() == 1
+    assert lbrr.lib().lbrr_abi_version() == 2
     d = lbrr.default_model()
     assert (d.dim, d.depth, d.heads, d.dim_head, d.num_stems, d.num_bands) == (256, 12, 8, 64, 6, 62)
     freqs = [d.freqs_per_band[i] for i in range(62)]

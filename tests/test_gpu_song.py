@@ -79,6 +79,26 @@ def test_short_song_and_serial_plan(weights):
         e0.close()
 
 
+def test_hann50_plan_matches_oracle(weights):
+    """BASELINE config 4's plan (50 % overlap, Hann-weighted overlap-add) through
+    lbrr_separate_song with one and two engines: bit-equal to the oracle's
+    chunk-order demix with the same per-chunk model and the same fp32 window."""
+    import lbrr
+    e0, e1 = _engine(0, weights), _engine(0, weights)
+    try:
+        audio = R.synth_audio(900000, seed=29)  # 4 chunks of the 50 % plan
+        p = dict(lbrr.HANN50)
+        one = lbrr.separate([e0], audio, **p)
+        two = lbrr.separate([e0, e1], audio, **p)
+        fade = p.pop("fade")
+        ref = R.demix(lambda c: e0.forward_host(np.ascontiguousarray(c.T)), audio, **p, fade_kind=fade)
+        assert np.array_equal(one, ref)
+        assert np.array_equal(two, ref)
+    finally:
+        e1.close()
+        e0.close()
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpus_match_one(weights):
     import lbrr

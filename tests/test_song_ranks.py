@@ -29,30 +29,31 @@ def fake_model(xc: np.ndarray) -> np.ndarray:
     return (xc[None] * gains + pos * np.float32(0.01)).astype(np.float32)
 
 
-def _worker(rank, world, init, audio, out_path, fail_rank):
+def _worker(rank, world, init, audio, out_path, fail_rank, plan):
     import torch
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=10))
+                            timeout=datetime.timedelta(seconds=30))
     try:
         def forward(x, y):
             if rank == fail_rank:
                 raise RuntimeError(f"rank {rank}: injected chunk failure")
             y.copy_(torch.from_numpy(fake_model(x.numpy().T.copy())))
 
-        res = song.separate_ranks(forward, audio, rank, world, dist, "cpu", **PLAN)
+        res = song.separate_ranks(forward, audio, rank, world, dist, "cpu", **plan)
         if rank == 0:
             np.save(out_path, res)
     finally:
         dist.destroy_process_group()
 
 
-def _run(world, tmp_path, audio, fail_rank=-1):
+def _run(world, tmp_path, audio, fail_rank=-1, plan=PLAN):
     out = tmp_path / f"song_w{world}.npy"
     # rendezvous through a file in the test's own directory: no port to race for
     init = f"file://{tmp_path / f'store_w{world}_f{fail_rank}'}"
     ctx = mp.get_context("spawn")
-    procs = [ctx.Process(target=_worker, args=(r, world, init, audio, str(out), fail_rank)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, init, audio, str(out), fail_rank, plan))
+             for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -86,6 +87,13 @@ def test_plan_matches_oracle():
         if i == n - 1:
             f[-1024:] = 1
         assert np.array_equal(w, f)
+        w = song.chunk_weights(i, n, 8192, 4096, "hann")
+        f = R.hann_fade(8192).copy()
+        if i == 0:
+            f[:4096] = 1
+        if i == n - 1:
+            f[-4096:] = 1
+        assert np.array_equal(w, f)
     x = np.arange(10, dtype=np.float32)[None]
     assert np.array_equal(song.reflect_pad(x, 25, 31), R.reflect_pad(x, 25, 31))
     with pytest.raises(ValueError):
@@ -107,10 +115,26 @@ def test_single_process(audio, expected):
 
 @pytest.mark.parametrize("world", [2, 3])
 def test_ranks_bit_identical(world, tmp_path, audio, expected):
+    """The overlap-strip exchange between ranks (the library's lbrr_separate_song
+    scheme) gives the chunk-order demix bit for bit."""
     out, codes = _run(world, tmp_path, audio)
     assert codes == [0] * world, codes
     got = np.load(out)
     assert np.array_equal(got, expected)
+
+
+HANN50 = dict(chunk=8192, step=4096, border=4096, fade="hann")
+DENSE = dict(chunk=8192, step=2048, border=1024)  # chunks overlap by more than half: gathered on rank 0
+
+
+@pytest.mark.parametrize("plan", [HANN50, DENSE], ids=["hann50", "dense"])
+def test_other_plans_bit_identical(plan, tmp_path, audio):
+    p = dict(plan)
+    fade = p.pop("fade", "linear")
+    want = R.demix(fake_model, audio, **p, fade_kind=fade)
+    out, codes = _run(2, tmp_path, audio, plan=plan)
+    assert codes == [0, 0], codes
+    assert np.array_equal(np.load(out), want)
 
 
 def test_failed_rank_fails_fast(tmp_path, audio):
