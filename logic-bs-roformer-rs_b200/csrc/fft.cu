@@ -86,8 +86,9 @@ __device__ __forceinline__ void dft32(float2 (&v)[32]) {
   }
 }
 
-// tw[k] = exp(+2 pi i k / 2048) for k in [0, 2048).
-__device__ __forceinline__ float2 twiddle(const float2* tw, int k) { return tw[k & (kTwN - 1)]; }
+// tw[k] = exp(+2 pi i k / 2048) for k in [0, 2048): a 16 KB table in global
+// memory, read through the read-only data cache (it stays L1-resident).
+__device__ __forceinline__ float2 twiddle(const float2* tw, int k) { return __ldg(tw + (k & (kTwN - 1))); }
 
 // 1024-point complex FFT of one frame by one warp.  On entry lane b holds
 // v[a] = input[32a + b]; on return lane c holds v[i] = output[c + 32 *
@@ -113,30 +114,28 @@ __device__ __forceinline__ void fft1024_warp(float2 (&v)[32], float2* xp, const 
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Front end: frames t0 .. t0+3 of both channels per CTA (8 warps: warp
-// = 2 * frame + channel), then band RMSNorm of all bands of those frames.
+// Front end: two frames per CTA, both channels (4 warps: warp = 2 * frame +
+// channel, each owning one 8.4 KB shared-memory slot that holds its transpose,
+// then Z, then the spectrum X in place), then the band RMSNorm of the 62 bands
+// of both frames.  34 KB of shared memory per CTA: six CTAs per SM.
 // ---------------------------------------------------------------------------
-constexpr int kFrontFrames = 4;
-constexpr int kFrontThreads = 2 * kFrontFrames * 32;
-constexpr int kFrontSpec = 1028;  // per (frame, channel) spectrum slot in shared memory (1025 used)
-constexpr int kFrontSmem = (kTwN + 2 * kFrontFrames * (kXpose + kFrontSpec)) * 8;
+constexpr int kFrontFrames = 2;
+constexpr int kFrontWarps = 2 * kFrontFrames;
+constexpr int kFrontSmem = kFrontWarps * kXpose * 8;
 
-__global__ void __launch_bounds__(kFrontThreads) stft_front_kernel(const float* __restrict__ x,
-                                                                   const float* __restrict__ win,
-                                                                   const float2* __restrict__ twg,
-                                                                   float2* __restrict__ spec,
-                                                                   const float* __restrict__ gamma,
-                                                                   const int* __restrict__ tab, __half* __restrict__ xn,
-                                                                   int xn_cols, int len, int T, int nb) {
+__global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const float* __restrict__ x,
+                                                                     const float* __restrict__ win,
+                                                                     const float2* __restrict__ tw,
+                                                                     float2* __restrict__ spec,
+                                                                     const float* __restrict__ gamma,
+                                                                     const int* __restrict__ tab,
+                                                                     __half* __restrict__ xn, int xn_cols, int len,
+                                                                     int T, int nb) {
   extern __shared__ __align__(16) float2 fsm[];
-  float2* tw = fsm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kTwN; i += blockDim.x) tw[i] = twg[i];
-  __syncthreads();
   const int fl = warp >> 1, ch = warp & 1;
   const int t = blockIdx.x * kFrontFrames + fl;
-  float2* xp = fsm + kTwN + warp * kXpose;
-  float2* xs = fsm + kTwN + 2 * kFrontFrames * kXpose + warp * kFrontSpec;
+  float2* xp = fsm + warp * kXpose;
   if (t < T) {
     // z[m] = x[2m] + i x[2m+1] of the windowed, reflect-padded frame; lane b loads z[32a + b]
     float2 v[32];
@@ -154,79 +153,67 @@ __global__ void __launch_bounds__(kFrontThreads) stft_front_kernel(const float* 
       v[a] = make_float2(s2[0], s2[1]);
     }
     fft1024_warp<false>(v, xp, tw, lane);
-    // Z[c + 32 d] (d = bitrev5(i)) into the transpose buffer, linear order
-    __syncwarp();
+    // Z[c + 32 d] (d = bitrev5(i)) into the slot, linear order
 #pragma unroll
     for (int i = 0; i < 32; ++i) xp[lane + 32 * bitrev5(i)] = v[i];
     __syncwarp();
-    // split step: X[k] for k = lane + 32 j, and X[1024]
-    float2* out = spec + (static_cast<size_t>(ch) * T + t) * kBins;
-#pragma unroll 4
-    for (int j = 0; j < 32; ++j) {
-      const int k = lane + 32 * j;
-      const float2 z = xp[k], zc = cconj(xp[(kBins - 1 - k) & 1023]);
+    // split step in place, one (k, 1024 - k) pair per lane and iteration:
+    //   X[k] = E + W^k O,  X[1024-k] = conj E - exp(+2 pi i k / 2048) conj O
+    for (int k = lane; k <= 512; k += 32) {
+      const float2 z = xp[k], zr = xp[(1024 - k) & 1023];
+      const float2 zc = cconj(zr);
       const float2 e = make_float2(0.5f * (z.x + zc.x), 0.5f * (z.y + zc.y));
       const float2 d = make_float2(0.5f * (z.x - zc.x), 0.5f * (z.y - zc.y));
       const float2 o = make_float2(d.y, -d.x);  // d / i
-      const float2 w = cconj(twiddle(tw, k));   // exp(-2 pi i k / 2048)
-      const float2 X = cadd(e, cmul(o, w));
-      xs[k] = X;
-      out[k] = X;
+      const float2 w = twiddle(tw, k);          // exp(+2 pi i k / 2048)
+      const float2 Xk = cadd(e, cmul(o, cconj(w)));
+      if (k == 0) {
+        xp[0] = make_float2(z.x + z.y, 0.f);     // E[0] + O[0]
+        xp[1024] = make_float2(z.x - z.y, 0.f);  // E[0] - O[0]
+      } else {
+        xp[k] = Xk;
+        if (k != 512) xp[1024 - k] = csub(cconj(e), cmul(w, cconj(o)));
+      }
     }
-    if (lane == 0) {
-      const float2 z0 = xp[0];
-      const float2 X = make_float2(z0.x - z0.y, 0.f);  // E[0] - O[0]
-      xs[1024] = X;
-      out[1024] = X;
-    }
+    __syncwarp();
+    float2* out = spec + (static_cast<size_t>(ch) * T + t) * kBins;
+    for (int k = lane; k < kBins; k += 32) out[k] = xp[k];
   }
   __syncthreads();
-  // band RMSNorm: one warp per (frame, band) of this CTA (bandsplit_norm:
-  // v * sqrt(d_b) / max(|v|, 1e-12) * gamma, zero-padded to the band's slot)
-  for (int task = warp; task < kFrontFrames * nb; task += 2 * kFrontFrames) {
+  // band RMSNorm (bandsplit_norm: v * sqrt(d_b) / max(|v|, 1e-12) * gamma,
+  // zero-padded to the band's 64-aligned slot), one warp per (frame, band):
+  // the sum of squares strided by lane, then the fp16 row two columns a lane
+  for (int task = warp; task < kFrontFrames * nb; task += kFrontWarps) {
     const int f = task / nb, b = task - f * nb;
     const int tt = blockIdx.x * kFrontFrames + f;
     if (tt >= T) continue;
     const int d = tab[b * 8 + 0], f0 = tab[b * 8 + 1], koff = tab[b * 8 + 2], kpad = tab[b * 8 + 3],
               goff = tab[b * 8 + 4];
-    const float2* s0 = fsm + kTwN + 2 * kFrontFrames * kXpose + (2 * f) * kFrontSpec;
-    float vals[17];
+    const float* s0 = reinterpret_cast<const float*>(fsm + (2 * f) * kXpose);
+    auto value = [&](int j) {  // x_in[j] of this band: spectrum bin f0 + j/4, channel (j/2)%2, re/im j%2
+      return s0[((j >> 1) & 1) * (2 * kXpose) + 2 * (f0 + (j >> 2)) + (j & 1)];
+    };
     float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 17; ++i) {
-      const int j = lane + 32 * i;
-      float vv = 0.f;
-      if (j < d) {
-        const float2 s = s0[((j >> 1) & 1) * kFrontSpec + f0 + (j >> 2)];
-        vv = (j & 1) ? s.y : s.x;
-      }
-      vals[i] = vv;
+    for (int j = lane; j < d; j += 32) {
+      const float vv = value(j);
       ss += vv * vv;
     }
     ss = warp_sum(ss);
     const float scale = sqrtf(static_cast<float>(d)) / fmaxf(sqrtf(ss), 1e-12f);
-    __half* row = xn + static_cast<long long>(tt) * xn_cols + koff;
-#pragma unroll
-    for (int i = 0; i < 17; ++i) {
-      const int j = lane + 32 * i;
-      if (j < kpad) {
-        const float vv = j < d ? __fmul_rn(__fmul_rn(vals[i], scale), __ldg(gamma + goff + j)) : 0.f;
-        row[j] = __float2half_rn(vv);
-      }
+    __half2* row = reinterpret_cast<__half2*>(xn + static_cast<long long>(tt) * xn_cols + koff);
+    for (int j = 2 * lane; j < kpad; j += 64) {
+      const float a0 = j < d ? __fmul_rn(__fmul_rn(value(j), scale), __ldg(gamma + goff + j)) : 0.f;
+      const float a1 = j + 1 < d ? __fmul_rn(__fmul_rn(value(j + 1), scale), __ldg(gamma + goff + j + 1)) : 0.f;
+      row[j >> 1] = __floats2half2_rn(a0, a1);
     }
-    for (int j = lane + 32 * 17; j < kpad; j += 32) row[j] = __float2half_rn(0.f);
   }
 }
 
 cudaError_t stft_front(const float* x, const float* window, const float2* twiddles, float2* spec, const float* gamma,
                        const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb, cudaStream_t st) {
-  static unsigned long long configured = 0;
-  cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(stft_front_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFrontSmem);
-  });
-  if (e != cudaSuccess) return e;
+  if ((xn_cols & 1) != 0) return cudaErrorInvalidValue;  // half2 row stores
   count_launch();
-  stft_front_kernel<<<(T + kFrontFrames - 1) / kFrontFrames, kFrontThreads, kFrontSmem, st>>>(
+  stft_front_kernel<<<(T + kFrontFrames - 1) / kFrontFrames, kFrontWarps * 32, kFrontSmem, st>>>(
       x, window, twiddles, spec, gamma, band_tab, xn, xn_cols, len, T, nb);
   return cudaGetLastError();
 }
@@ -234,34 +221,27 @@ cudaError_t stft_front(const float* x, const float* window, const float2* twiddl
 // ---------------------------------------------------------------------------
 // Back end: channel sc = blockIdx.y, output blocks [k0, k0 + kBackBlocks) of
 // 512 padded samples, k0 = 2 + blockIdx.x * kBackBlocks.  Frames k0-3 ..
-// k0+kBackBlocks-1 (16; two per warp) are inverse-transformed into shared
-// memory (x[n] * w[n], already divided by 2048), then every output sample sums
-// its (up to four) frames in frame order and takes the envelope.
+// k0+kBackBlocks-1 (one per warp) are inverse-transformed into shared memory
+// (x[n] * w[n], already divided by 2048), then every output sample sums its
+// (up to four) frames in frame order and takes the envelope.  12 warps and
+// 101 KB of shared memory per CTA: two CTAs per SM.
 // ---------------------------------------------------------------------------
-constexpr int kBackWarps = 8;
-constexpr int kBackFramesPerCta = 2 * kBackWarps;
-constexpr int kBackBlocks = kBackFramesPerCta - 3;
-constexpr int kBackSlot = kXpose;  // a frame's 2048 floats live in its (larger) transpose slot
-constexpr int kBackSmem = (kTwN + kBackFramesPerCta * kBackSlot) * 8;
+constexpr int kBackWarps = 12;
+constexpr int kBackBlocks = kBackWarps - 3;
+constexpr int kBackSmem = kBackWarps * kXpose * 8;
 
 __global__ void __launch_bounds__(kBackWarps * 32) istft_back_kernel(const float2* __restrict__ c2r,
                                                                      const float* __restrict__ win,
-                                                                     const float2* __restrict__ twg,
+                                                                     const float2* __restrict__ tw,
                                                                      const float* __restrict__ inv_env,
                                                                      float* __restrict__ out, int len, int T) {
   extern __shared__ __align__(16) float2 bsm[];
-  float2* tw = bsm;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sc = blockIdx.y;
   const int k0 = 2 + blockIdx.x * kBackBlocks;
-  for (int i = threadIdx.x; i < kTwN; i += blockDim.x) tw[i] = twg[i];
-  __syncthreads();
-#pragma unroll 1
-  for (int r = 0; r < 2; ++r) {
-    const int slot = warp + r * kBackWarps;
-    const int t = k0 - 3 + slot;
-    if (t < 0 || t >= T) continue;
-    float2* xp = bsm + kTwN + slot * kBackSlot;
+  const int t = k0 - 3 + warp;
+  if (t >= 0 && t < T) {
+    float2* xp = bsm + warp * kXpose;
     const float2* X = c2r + (static_cast<size_t>(sc) * T + t) * kBins;
     // Z'[k] = (X[k] + conj X[1024-k]) + i (X[k] - conj X[1024-k]) exp(+2 pi i k / 2048),
     // DC and Nyquist taken as real; lane b builds Z'[32a + b]
@@ -281,7 +261,6 @@ __global__ void __launch_bounds__(kBackWarps * 32) istft_back_kernel(const float
     }
     fft1024_warp<true>(v, xp, tw, lane);
     // y[c + 32 d] = 2048 (x[2m] + i x[2m+1]), m = c + 32 d: windowed samples into the slot
-    __syncwarp();
     float* fr = reinterpret_cast<float*>(xp);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
@@ -300,10 +279,10 @@ __global__ void __launch_bounds__(kBackWarps * 32) istft_back_kernel(const float
     float sum = 0.f;
 #pragma unroll
     for (int q = 3; q >= 0; --q) {
-      const int t = k - q;
-      if (t < 0 || t >= T) continue;
-      const float* fr = reinterpret_cast<const float*>(bsm + kTwN + (t - (k0 - 3)) * kBackSlot);
-      sum += fr[p - t * kHop];
+      const int tq = k - q;
+      if (tq < 0 || tq >= T) continue;
+      const float* fr = reinterpret_cast<const float*>(bsm + (tq - (k0 - 3)) * kXpose);
+      sum += fr[p - tq * kHop];
     }
     o[p - kNfft / 2] = sum * __ldg(inv_env + p);
   }

@@ -679,18 +679,7 @@ struct EpiRow256 : DenseTiles {
       if (tid < 8) c[kRowGateB + tid] = __ldg(np.gate_b + tid);
     }
   }
-  // The next tile's fp32 residual (128 rows x 1 KB) into L2 while this tile's
-  // epilogue runs: thread (part, row) asks for its half row, four 128-byte
-  // lines, so the residual reads one tile later hit L2 instead of HBM.
-  __device__ void prefetch_resid(const TileDesc& t, const EpiCtx& x) const {
-    if (!resid || x.row >= t.rows) return;
-    const char* rp = reinterpret_cast<const char*>(resid + static_cast<size_t>(t.row0 + x.row) * 256 + x.c0);
-#pragma unroll
-    for (int k = 0; k < kPartCols * 4 / 128; ++k) prefetch_l2(rp + k * 128);
-  }
-  __device__ void prefetch(const TileDesc& t, EpiCtx& x) const { prefetch_resid(t, x); }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
-    if (x.next_tile >= 0) prefetch_resid(tile(x.next_tile), x);
     row256_epilogue<false, true>(t, x, bias, resid, maps, np, 0, [&](int r) { return t.row0 + r; });
   }
 };
@@ -759,28 +748,7 @@ struct EpiMask : TableTiles {
   float2* out;          // [stems*2][T][1025]
   int T, n2tot;
   int keep_dc_imag;     // 1: the DC/Nyquist bins keep the imaginary part the complex mask gives them
-  // The spectrum bins of the next tile (both channels of each of its frames,
-  // this warp's share of the band's bins) into L2 during this tile: the
-  // hidden-layer stream evicts them between the six stems' passes.
-  __device__ void prefetch_spec(const TileDesc& t, const EpiCtx& x) const {
-    if (x.row >= t.rows) return;
-    const int band = (t.aux >> 8) & 255, n0 = (t.aux & 255) * kBN;
-    const int d_b = band_d[band], f0 = band_f0[band];
-    // columns [n0 + c0, n0 + c0 + kPartCols) of the permuted (a, g) pairs cover bins (col >> 3)
-    const int b_lo = (n0 + x.c0) >> 3, b_hi = min((n0 + x.c0 + kPartCols) >> 3, d_b >> 2);
-    if (b_lo >= b_hi) return;
-    for (int ch = 0; ch < 2; ++ch) {
-      const char* lo = reinterpret_cast<const char*>(spec + (static_cast<size_t>(ch) * T + t.row0 + x.row) * 1025 +
-                                                     f0 + b_lo);
-      const char* hi = reinterpret_cast<const char*>(spec + (static_cast<size_t>(ch) * T + t.row0 + x.row) * 1025 +
-                                                     f0 + b_hi);
-      for (const char* q = reinterpret_cast<const char*>(reinterpret_cast<uintptr_t>(lo) & ~uintptr_t(127)); q < hi;
-           q += 128)
-        prefetch_l2(q);
-    }
-  }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
-    if (x.next_tile >= 0) prefetch_spec(table[x.next_tile], x);
     const bool valid = x.row < t.rows;
     const int rb = x.q * 32;                // this warp's first tile row
     const int rows_valid = min(32, t.rows - rb);
