@@ -114,16 +114,16 @@ __device__ __forceinline__ void fft1024_warp(float2 (&v)[32], float2* xp, const 
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Front end: two frames per CTA, both channels (4 warps: warp = 2 * frame +
-// channel, each owning one 8.4 KB shared-memory slot that holds its transpose,
-// then Z, then the spectrum X in place), then the band RMSNorm of the 62 bands
-// of both frames.  34 KB of shared memory per CTA: six CTAs per SM.
+// Front end: one frame per CTA of four warps.  Warps 0 and 1 transform the two
+// channels (each owning one 8.4 KB shared-memory slot that holds its
+// transpose, then Z, then the spectrum X in place); then all four warps run
+// the band RMSNorm of the frame's 62 bands.  17 KB of shared memory and at
+// most 96 registers a thread: five CTAs per SM.
 // ---------------------------------------------------------------------------
-constexpr int kFrontFrames = 2;
-constexpr int kFrontWarps = 2 * kFrontFrames;
-constexpr int kFrontSmem = kFrontWarps * kXpose * 8;
+constexpr int kFrontWarps = 4;
+constexpr int kFrontSmem = 2 * kXpose * 8 + kNumBands * 8 * 4;
 
-__global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const float* __restrict__ x,
+__global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const float* __restrict__ x,
                                                                      const float* __restrict__ win,
                                                                      const float2* __restrict__ tw,
                                                                      float2* __restrict__ spec,
@@ -132,25 +132,28 @@ __global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const floa
                                                                      __half* __restrict__ xn, int xn_cols, int len,
                                                                      int T, int nb) {
   extern __shared__ __align__(16) float2 fsm[];
+  int* stab = reinterpret_cast<int*>(fsm + 2 * kXpose);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int fl = warp >> 1, ch = warp & 1;
-  const int t = blockIdx.x * kFrontFrames + fl;
-  float2* xp = fsm + warp * kXpose;
-  if (t < T) {
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < nb * 8; i += blockDim.x) stab[i] = __ldg(tab + i);
+  if (warp < 2) {
+    const int ch = warp;
+    float2* xp = fsm + warp * kXpose;
     // z[m] = x[2m] + i x[2m+1] of the windowed, reflect-padded frame; lane b loads z[32a + b]
     float2 v[32];
     const int pad = kNfft / 2;
 #pragma unroll
     for (int a = 0; a < 32; ++a) {
       const int j = 64 * a + 2 * lane;
+      const float2 w2 = __ldg(reinterpret_cast<const float2*>(win) + (j >> 1));
       float s2[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int g = t * kHop + j + e;
         const int src = g < pad ? pad - g : (g >= len + pad ? 2 * len + pad - 2 - g : g - pad);
-        s2[e] = __ldg(x + 2ll * src + ch) * __ldg(win + j + e);
+        s2[e] = __ldg(x + 2ll * src + ch);
       }
-      v[a] = make_float2(s2[0], s2[1]);
+      v[a] = make_float2(s2[0] * w2.x, s2[1] * w2.y);
     }
     fft1024_warp<false>(v, xp, tw, lane);
     // Z[c + 32 d] (d = bitrev5(i)) into the slot, linear order
@@ -181,15 +184,12 @@ __global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const floa
   }
   __syncthreads();
   // band RMSNorm (bandsplit_norm: v * sqrt(d_b) / max(|v|, 1e-12) * gamma,
-  // zero-padded to the band's 64-aligned slot), one warp per (frame, band):
-  // the sum of squares strided by lane, then the fp16 row two columns a lane
-  for (int task = warp; task < kFrontFrames * nb; task += kFrontWarps) {
-    const int f = task / nb, b = task - f * nb;
-    const int tt = blockIdx.x * kFrontFrames + f;
-    if (tt >= T) continue;
-    const int d = tab[b * 8 + 0], f0 = tab[b * 8 + 1], koff = tab[b * 8 + 2], kpad = tab[b * 8 + 3],
-              goff = tab[b * 8 + 4];
-    const float* s0 = reinterpret_cast<const float*>(fsm + (2 * f) * kXpose);
+  // zero-padded to the band's 64-aligned slot), one warp per band: the sum of
+  // squares strided by lane, then the fp16 row two columns a lane
+  const float* s0 = reinterpret_cast<const float*>(fsm);
+  for (int b = warp; b < nb; b += kFrontWarps) {
+    const int d = stab[b * 8 + 0], f0 = stab[b * 8 + 1], koff = stab[b * 8 + 2], kpad = stab[b * 8 + 3],
+              goff = stab[b * 8 + 4];
     auto value = [&](int j) {  // x_in[j] of this band: spectrum bin f0 + j/4, channel (j/2)%2, re/im j%2
       return s0[((j >> 1) & 1) * (2 * kXpose) + 2 * (f0 + (j >> 2)) + (j & 1)];
     };
@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const floa
     }
     ss = warp_sum(ss);
     const float scale = sqrtf(static_cast<float>(d)) / fmaxf(sqrtf(ss), 1e-12f);
-    __half2* row = reinterpret_cast<__half2*>(xn + static_cast<long long>(tt) * xn_cols + koff);
+    __half2* row = reinterpret_cast<__half2*>(xn + static_cast<long long>(t) * xn_cols + koff);
     for (int j = 2 * lane; j < kpad; j += 64) {
       const float a0 = j < d ? __fmul_rn(__fmul_rn(value(j), scale), __ldg(gamma + goff + j)) : 0.f;
       const float a1 = j + 1 < d ? __fmul_rn(__fmul_rn(value(j + 1), scale), __ldg(gamma + goff + j + 1)) : 0.f;
@@ -211,10 +211,10 @@ __global__ void __launch_bounds__(kFrontWarps * 32) stft_front_kernel(const floa
 
 cudaError_t stft_front(const float* x, const float* window, const float2* twiddles, float2* spec, const float* gamma,
                        const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb, cudaStream_t st) {
-  if ((xn_cols & 1) != 0) return cudaErrorInvalidValue;  // half2 row stores
+  if ((xn_cols & 1) != 0 || nb > kNumBands) return cudaErrorInvalidValue;  // half2 row stores, table size
   count_launch();
-  stft_front_kernel<<<(T + kFrontFrames - 1) / kFrontFrames, kFrontWarps * 32, kFrontSmem, st>>>(
-      x, window, twiddles, spec, gamma, band_tab, xn, xn_cols, len, T, nb);
+  stft_front_kernel<<<T, kFrontWarps * 32, kFrontSmem, st>>>(x, window, twiddles, spec, gamma, band_tab, xn,
+                                                             xn_cols, len, T, nb);
   return cudaGetLastError();
 }
 
@@ -230,7 +230,7 @@ constexpr int kBackWarps = 12;
 constexpr int kBackBlocks = kBackWarps - 3;
 constexpr int kBackSmem = kBackWarps * kXpose * 8;
 
-__global__ void __launch_bounds__(kBackWarps * 32) istft_back_kernel(const float2* __restrict__ c2r,
+__global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const float2* __restrict__ c2r,
                                                                      const float* __restrict__ win,
                                                                      const float2* __restrict__ tw,
                                                                      const float* __restrict__ inv_env,
@@ -292,7 +292,11 @@ cudaError_t istft_back(const float2* c2r, const float* window, const float2* twi
                        float* out, int len, int T, int channels, cudaStream_t st) {
   static unsigned long long configured = 0;
   cudaError_t e = once_per_device(configured, [] {
-    return cudaFuncSetAttribute(istft_back_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBackSmem);
+    cudaError_t r = cudaFuncSetAttribute(istft_back_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBackSmem);
+    // the whole unified L1/shared array as shared memory: two CTAs per SM
+    if (r == cudaSuccess)
+      r = cudaFuncSetAttribute(istft_back_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return r;
   });
   if (e != cudaSuccess) return e;
   const int k_last = (len + kNfft / 2 - 1) / kHop;  // last output block
