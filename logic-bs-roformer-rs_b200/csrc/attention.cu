@@ -212,113 +212,70 @@ __global__ void __launch_bounds__(kT1Threads, 2)
       tc_fence_after();
       const int hi = min(128, T - j * 128);  // valid keys of this tile: [0, hi)
       uint32_t s_row[2][64];
+      tmem_ld64(tS, s_row[0]);
+      tmem_ld64(tS + 64, s_row[1]);
+      tmem_ld_wait64(s_row[0]);
+      tmem_ld_wait64(s_row[1]);
       uint32_t(&s)[4][32] = *reinterpret_cast<uint32_t(*)[4][32]>(s_row);
-      auto mask_half = [&](int h) {  // keys >= hi among columns [64h, 64h + 64)
-        if (hi < 128) {
+      // S is in registers: the MMA warp may overwrite it with the next tile
+      tc_fence_before();
+      mbar_arrive(s_free);
+      if (hi < 128) {
 #pragma unroll
-          for (int q4 = 2 * h; q4 < 2 * h + 2; ++q4)
+        for (int q4 = 0; q4 < 4; ++q4)
 #pragma unroll
-            for (int k = 0; k < 32; ++k)
-              if (q4 * 32 + k >= hi) s[q4][k] = __float_as_uint(-INFINITY);
-        }
-      };
-      // Row max in eight independent chains of three-input max (chain c covers
-      // 16 columns), optionally fused into the exponential loop.  P leaves for
-      // TMEM in two 32-column halves (w holds one half).
+          for (int k = 0; k < 32; ++k)
+            if (q4 * 32 + k >= hi) s[q4][k] = __float_as_uint(-INFINITY);
+      }
+      // row max: eight independent chains of three-input max, then a tree
       float mq[8];
-      uint32_t w[32];
-      float2 sum2[4];
-      auto exp_half = [&](int h, float msc, bool track) {
 #pragma unroll
-        for (int q4 = 2 * h; q4 < 2 * h + 2; ++q4) {
+      for (int c = 0; c < 8; ++c) {
+        const uint32_t* v = &s[c >> 1][(c & 1) * 16];
+        float m = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            const float e0 = __uint_as_float(s[q4][2 * k]), e1 = __uint_as_float(s[q4][2 * k + 1]);
-            if (track) mq[q4 * 2 + (k >> 3)] = max3f(mq[q4 * 2 + (k >> 3)], e0, e1);
-            const float2 a2 = __ffma2_rn(make_float2(e0, e1), make_float2(sc, sc), make_float2(-msc, -msc));
-            // 5 of every 16 pairs on the FMA pipe, the rest on MUFU
-            const float2 p = k >= 11 ? exp2_poly2(a2) : make_float2(ex2(a2.x), ex2(a2.y));
-            sum2[k & 3] = __fadd2_rn(sum2[k & 3], p);
-            w[(q4 - 2 * h) * 16 + k] = pack_f16x2(p.x, p.y);
-          }
-        }
-      };
-      auto zero_sums = [&]() {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sum2[i] = make_float2(0.f, 0.f);
-      };
-      auto wait_pv = [&]() {  // O += P(j-1) V(j-1) done: P may be rewritten, O rescaled
-        if (j == 0) return true;
-        if (!mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status)) return false;
-        tc_fence_after();
-        return true;
-      };
+        for (int k = 3; k < 15; k += 2) m = max3f(m, __uint_as_float(v[k]), __uint_as_float(v[k + 1]));
+        mq[c] = fmaxf(m, __uint_as_float(v[15]));
+      }
+      const float mx = max3f(max3f(mq[0], mq[1], mq[2]), max3f(mq[3], mq[4], mq[5]), fmaxf(mq[6], mq[7]));
+      const float m_new = fmaxf(m_run, mx);
       // Keep the running reference max unless the row max grew by more than
       // 2^8 in exp2 units (exponents stay <= 2^8 in fp32 and in the fp16 P),
       // so O needs no rescale on most tiles.
-      float corr = 1.0f, m_next = m_run;
-      zero_sums();
-      if (j == 0) {
-        // first tile: the row max comes first
-        tmem_ld64(tS, s_row[0]);
-        tmem_ld64(tS + 64, s_row[1]);
-        tmem_ld_wait64(s_row[0]);
-        tmem_ld_wait64(s_row[1]);
-        // S is in registers: the MMA warp may overwrite it with the next tile
-        tc_fence_before();
-        mbar_arrive(s_free);
-        mask_half(0);
-        mask_half(1);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          const uint32_t* v = &s[c >> 1][(c & 1) * 16];
-          float m = max3f(__uint_as_float(v[0]), __uint_as_float(v[1]), __uint_as_float(v[2]));
-#pragma unroll
-          for (int k = 3; k < 15; k += 2) m = max3f(m, __uint_as_float(v[k]), __uint_as_float(v[k + 1]));
-          mq[c] = fmaxf(m, __uint_as_float(v[15]));
-        }
-        const float mx = max3f(max3f(mq[0], mq[1], mq[2]), max3f(mq[3], mq[4], mq[5]), fmaxf(mq[6], mq[7]));
-        const float m_new = fmaxf(m_run, mx);
-        const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      float m_use, corr, m_next;
+      if (m_run == -INFINITY || (m_new - m_run) * sc > 8.0f) {
+        m_use = m_new == -INFINITY ? 0.f : m_new;
         corr = ex2((m_run - m_use) * sc);
         m_next = m_new;
-        exp_half(0, m_use * sc, false);
-        tmem_st32(tP, w);
-        exp_half(1, m_use * sc, false);
       } else {
-        // Later tiles: exponentiate against the running max straight away (the
-        // row max is folded into the same loop) while the second half of S is
-        // still loading.  If some row's max grew by more than 2^8 the warp redoes
-        // the tile against the new max (rows whose max did not grow recompute
-        // the same values), so the result equals taking the max first.
+        m_use = m_run;
+        corr = 1.0f;
+        m_next = m_run;
+      }
+      const float msc = m_use * sc;
+      uint32_t w[64];
+      float2 sum2[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
-        for (int c = 0; c < 8; ++c) mq[c] = -INFINITY;
-        const float msc = m_run * sc;
-        tmem_ld64(tS, s_row[0]);
-        tmem_ld_wait64(s_row[0]);
-        tmem_ld64(tS + 64, s_row[1]);
-        mask_half(0);
-        exp_half(0, msc, true);
-        ok = __all_sync(0xffffffffu, wait_pv());  // the warp leaves the loop together on a timeout
-        tmem_st32(tP, w);
-        tmem_ld_wait64(s_row[1]);
-        tc_fence_before();
-        mbar_arrive(s_free);
+      for (int q4 = 0; q4 < 4; ++q4) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+          const float2 a2 = __ffma2_rn(make_float2(__uint_as_float(s[q4][2 * k]), __uint_as_float(s[q4][2 * k + 1])),
+                                       make_float2(sc, sc), make_float2(-msc, -msc));
+          // 5 of every 16 pairs on the FMA pipe, the rest on MUFU
+          const float2 p = k >= 11 ? exp2_poly2(a2) : make_float2(ex2(a2.x), ex2(a2.y));
+          sum2[k & 3] = __fadd2_rn(sum2[k & 3], p);
+          w[q4 * 16 + k] = pack_f16x2(p.x, p.y);
+        }
+      }
+      const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
+      const float sum = sa.x + sa.y;
+      if (j > 0) {
+        // O += P(j-1) V(j-1) must be complete before O is rescaled and P
+        // rewritten
+        ok = mbar_wait(o_done, (j - 1) & 1, abort_flag, a.status);
         if (!ok) break;
-        mask_half(1);
-        exp_half(1, msc, true);
-        const float mx = max3f(max3f(mq[0], mq[1], mq[2]), max3f(mq[3], mq[4], mq[5]), fmaxf(mq[6], mq[7]));
-        const float m_new = fmaxf(m_run, mx);
-        const bool grow = (m_new - m_run) * sc > 8.0f;
-        if (__any_sync(0xffffffffu, grow)) {
-          const float m_use = grow ? m_new : m_run;
-          corr = grow ? ex2((m_run - m_new) * sc) : 1.0f;
-          m_next = m_use;
-          zero_sums();
-          exp_half(0, m_use * sc, false);
-          tmem_st32(tP, w);
-          exp_half(1, m_use * sc, false);
-          // rescale O by corr (1 for the rows whose max did not grow)
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, corr != 1.0f)) {
 #pragma unroll 1
           for (int c = 0; c < 64; c += 32) {
             uint32_t v[32];
@@ -333,12 +290,11 @@ __global__ void __launch_bounds__(kT1Threads, 2)
             }
             tmem_st32(tO + c, v);
           }
+          tmem_st_wait();
         }
       }
-      tmem_st32(tP + 32, w);
+      tmem_st64(tP, w);
       tmem_st_wait();
-      const float2 sa = __fadd2_rn(__fadd2_rn(sum2[0], sum2[1]), __fadd2_rn(sum2[2], sum2[3]));
-      const float sum = sa.x + sa.y;
       l_run = l_run * corr + sum;
       m_run = m_next;
       tc_fence_before();
