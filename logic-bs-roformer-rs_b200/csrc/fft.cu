@@ -86,13 +86,23 @@ __device__ __forceinline__ void dft32(float2 (&v)[32]) {
   }
 }
 
-// tw[k] = exp(+2 pi i k / 2048) for k in [0, 2048): a 16 KB table in global
-// memory, read through the read-only data cache (it stays L1-resident).
-__device__ __forceinline__ float2 twiddle(const float2* tw, int k) { return __ldg(tw + (k & (kTwN - 1))); }
+// Twiddles come from a per-CTA shared-memory copy of tws[k] = exp(+2 pi i k /
+// 2048) for k in [0, 1024) (8 KB; the second half of the circle is the first
+// negated).
+constexpr int kTwS = 1024;
+__device__ __forceinline__ float2 twiddle(const float2* tws, int k) {
+  const float2 w = tws[k & (kTwS - 1)];
+  return (k & kTwS) ? make_float2(-w.x, -w.y) : w;
+}
+// Copy the first kTwS entries of the global table into shared memory.
+__device__ __forceinline__ void load_twiddles(float2* tws, const float2* __restrict__ twg) {
+  for (int i = threadIdx.x; i < kTwS; i += blockDim.x) tws[i] = __ldg(twg + i);
+}
 
 // 1024-point complex FFT of one frame by one warp.  On entry lane b holds
 // v[a] = input[32a + b]; on return lane c holds v[i] = output[c + 32 *
-// bitrev5(i)].  `xp` is the warp's padded transpose buffer.
+// bitrev5(i)].  `xp` is the warp's padded transpose buffer, `tw` the shared
+// twiddle table.
 template <bool INV>
 __device__ __forceinline__ void fft1024_warp(float2 (&v)[32], float2* xp, const float2* tw, int lane) {
   dft32<INV>(v);
@@ -121,27 +131,41 @@ __device__ __forceinline__ void fft1024_warp(float2 (&v)[32], float2* xp, const 
 // most 96 registers a thread: five CTAs per SM.
 // ---------------------------------------------------------------------------
 constexpr int kFrontWarps = 4;
-constexpr int kFrontSmem = 2 * kXpose * 8 + kNumBands * 8 * 4;
+constexpr int kFrontSmem = 2 * kXpose * 8 + kTwS * 8 + kNumBands * 8 * 4;
 
 __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const float* __restrict__ x,
                                                                      const float* __restrict__ win,
-                                                                     const float2* __restrict__ tw,
+                                                                     const float2* __restrict__ twg,
                                                                      float2* __restrict__ spec,
                                                                      const float* __restrict__ gamma,
                                                                      const int* __restrict__ tab,
                                                                      __half* __restrict__ xn, int xn_cols, int len,
                                                                      int T, int nb) {
   extern __shared__ __align__(16) float2 fsm[];
-  int* stab = reinterpret_cast<int*>(fsm + 2 * kXpose);
+  float2* tw = fsm + 2 * kXpose;
+  int* stab = reinterpret_cast<int*>(tw + kTwS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
+  const int pad = kNfft / 2;
+  // Interior frames (no reflection) stage their 2048 interleaved stereo
+  // samples, 16 KB contiguous and 16-byte aligned, with coalesced 16-byte loads
+  // across both channels' slots; frames at the song edges gather per sample.
+  const bool interior = t * kHop >= pad && t * kHop + kNfft <= len + pad &&
+                        (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  if (interior) {
+    const float4* src = reinterpret_cast<const float4*>(x + 2ll * (t * kHop - pad));
+    float4* dst = reinterpret_cast<float4*>(fsm);
+    for (int i = threadIdx.x; i < kNfft / 2; i += blockDim.x) dst[i] = __ldg(src + i);
+  }
   for (int i = threadIdx.x; i < nb * 8; i += blockDim.x) stab[i] = __ldg(tab + i);
+  load_twiddles(tw, twg);
+  __syncthreads();
   if (warp < 2) {
     const int ch = warp;
     float2* xp = fsm + warp * kXpose;
     // z[m] = x[2m] + i x[2m+1] of the windowed, reflect-padded frame; lane b loads z[32a + b]
     float2 v[32];
-    const int pad = kNfft / 2;
+    const float* staged = reinterpret_cast<const float*>(fsm);
 #pragma unroll
     for (int a = 0; a < 32; ++a) {
       const int j = 64 * a + 2 * lane;
@@ -149,12 +173,18 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
       float s2[2];
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int g = t * kHop + j + e;
-        const int src = g < pad ? pad - g : (g >= len + pad ? 2 * len + pad - 2 - g : g - pad);
-        s2[e] = __ldg(x + 2ll * src + ch);
+        if (interior) {
+          s2[e] = staged[2 * (j + e) + ch];
+        } else {
+          const int g = t * kHop + j + e;
+          const int src = g < pad ? pad - g : (g >= len + pad ? 2 * len + pad - 2 - g : g - pad);
+          s2[e] = __ldg(x + 2ll * src + ch);
+        }
       }
       v[a] = make_float2(s2[0] * w2.x, s2[1] * w2.y);
     }
+    // both channels have read the staged samples before either slot is reused
+    asm volatile("bar.sync 1, 64;" ::: "memory");
     fft1024_warp<false>(v, xp, tw, lane);
     // Z[c + 32 d] (d = bitrev5(i)) into the slot, linear order
 #pragma unroll
@@ -228,28 +258,42 @@ cudaError_t stft_front(const float* x, const float* window, const float2* twiddl
 // ---------------------------------------------------------------------------
 constexpr int kBackWarps = 12;
 constexpr int kBackBlocks = kBackWarps - 3;
-constexpr int kBackSmem = kBackWarps * kXpose * 8;
+constexpr int kBackSmem = kBackWarps * kXpose * 8 + kTwS * 8;
 
 __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const float2* __restrict__ c2r,
                                                                      const float* __restrict__ win,
-                                                                     const float2* __restrict__ tw,
+                                                                     const float2* __restrict__ twg,
                                                                      const float* __restrict__ inv_env,
                                                                      float* __restrict__ out, int len, int T) {
   extern __shared__ __align__(16) float2 bsm[];
+  float2* tw = bsm + kBackWarps * kXpose;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sc = blockIdx.y;
   const int k0 = 2 + blockIdx.x * kBackBlocks;
   const int t = k0 - 3 + warp;
-  if (t >= 0 && t < T) {
-    float2* xp = bsm + warp * kXpose;
+  const bool has_frame = t >= 0 && t < T;
+  float2* xp = bsm + warp * kXpose;
+  int shift = 0;  // the frame's first bin inside the slot (0 or 1: 16-byte aligned loads)
+  if (has_frame) {
+    // the frame's 1025 bins into its slot with coalesced 16-byte loads: the
+    // 16-byte-aligned span holding them (at most 8 bytes before and after)
     const float2* X = c2r + (static_cast<size_t>(sc) * T + t) * kBins;
+    shift = static_cast<int>((reinterpret_cast<uintptr_t>(X) >> 3) & 1);
+    const float4* src = reinterpret_cast<const float4*>(X - shift);
+    float4* dst = reinterpret_cast<float4*>(xp);
+    for (int i = lane; i < (shift + kBins + 1) / 2; i += 32) dst[i] = __ldg(src + i);
+  }
+  load_twiddles(tw, twg);
+  __syncthreads();
+  if (has_frame) {
+    const float2* X = xp + shift;
     // Z'[k] = (X[k] + conj X[1024-k]) + i (X[k] - conj X[1024-k]) exp(+2 pi i k / 2048),
     // DC and Nyquist taken as real; lane b builds Z'[32a + b]
     float2 v[32];
 #pragma unroll
     for (int a = 0; a < 32; ++a) {
       const int k = 32 * a + lane;
-      float2 xk = __ldg(X + k), xr = __ldg(X + 1024 - k);
+      float2 xk = X[k], xr = X[1024 - k];
       if (k == 0) {
         xk.y = 0.f;
         xr.y = 0.f;
@@ -259,15 +303,17 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
       const float2 o = cmul(csub(xk, xc), twiddle(tw, k));
       v[a] = make_float2(e.x - o.y, e.y + o.x);  // e + i o
     }
+    __syncwarp();  // every lane has read the staged bins before the slot becomes the transpose buffer
     fft1024_warp<true>(v, xp, tw, lane);
-    // y[c + 32 d] = 2048 (x[2m] + i x[2m+1]), m = c + 32 d: windowed samples into the slot
+    // y[c + 32 d] = 2048 (x[2m] + i x[2m+1]), m = c + 32 d: windowed samples (still
+    // times 2048; the overlap-add scales once) into the slot
     float* fr = reinterpret_cast<float*>(xp);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
       const int m = lane + 32 * bitrev5(i);
       const float2 w2 = __ldg(reinterpret_cast<const float2*>(win) + m);
-      fr[2 * m] = (v[i].x * (1.0f / 2048.0f)) * w2.x;
-      fr[2 * m + 1] = (v[i].y * (1.0f / 2048.0f)) * w2.y;
+      fr[2 * m] = v[i].x * w2.x;
+      fr[2 * m + 1] = v[i].y * w2.y;
     }
   }
   __syncthreads();
@@ -284,7 +330,7 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
       const float* fr = reinterpret_cast<const float*>(bsm + (tq - (k0 - 3)) * kXpose);
       sum += fr[p - tq * kHop];
     }
-    o[p - kNfft / 2] = sum * __ldg(inv_env + p);
+    o[p - kNfft / 2] = sum * ((1.0f / 2048.0f) * __ldg(inv_env + p));
   }
 }
 
