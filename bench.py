@@ -304,6 +304,7 @@ def run_ours(args, rank, world, local_rank):
         for g in gemms.values():
             g["pct_of_peak"] = round(100.0 * g["tflops"] / pk["tflops"], 1)
         mask = time_mask_estimator(torch, eng, x, out, stream, flush, args)
+        dual = time_two_in_flight(torch, lbrr, eng, x, out, local_rank, args)
         short = time_short_chunk(torch, eng, stream, flush, args)
         wb, sb = eng.memory()
         result = {
@@ -329,6 +330,7 @@ def run_ours(args, rank, world, local_rank):
             "trunk_gemms": gemms,
             "short_chunk": short,
             "mask_estimator": mask,
+            "two_in_flight": dual,
             "chunk_rtf": round(ms / (CHUNK / SR * 1000.0), 6),
             "song": song,
             "clocks": clocks,
@@ -383,6 +385,48 @@ def time_short_chunk(torch, eng, stream, flush, args):
     eng.sync()
     return {"ms": round(ms, 4), "tflops": round(SHORT_FLOP / ms / 1e9, 1), "samples": L, "frames": 259,
             "published_rtx3080_ms": 33.81}
+
+
+def time_two_in_flight(torch, lbrr, eng, x, out, local_rank, args):
+    """Two chunks in flight on one GPU: a second engine on the same device, each
+    engine on its own stream, forwards issued alternately; ms per chunk over the
+    pairs (CUDA events, the second stream joined into the first), and the song
+    with both engines dealt chunks alternately."""
+    from lbrr import synthetic
+    e2 = lbrr.Engine(local_rank, CHUNK)
+    try:
+        e2.upload_weights(synthetic.checkpoint(seed=0))
+        out2 = torch.empty_like(out)
+        s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+        for _ in range(3):
+            eng.bench_forward(x, out, stream=s1)
+            e2.bench_forward(x, out2, stream=s2)
+        torch.cuda.synchronize()
+        pairs = max(2, min(args.steps, 10))
+        a, b, j = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+                   torch.cuda.Event())
+        a.record(s1)
+        s2.wait_event(a)
+        for _ in range(pairs):
+            eng.bench_forward(x, out, stream=s1)
+            e2.bench_forward(x, out2, stream=s2)
+        j.record(s2)
+        s1.wait_event(j)
+        b.record(s1)
+        torch.cuda.synchronize()
+        eng.sync()
+        e2.sync()
+        res = {"ms_per_chunk": round(a.elapsed_time(b) / (2 * pairs), 4), "pairs": pairs,
+               "how": "two engines on one GPU, one stream each, forwards issued alternately"}
+        from lbrr import song
+        audio_il = np.ascontiguousarray(synthetic.audio(SONG_LEN, seed=42).T)
+        stems = lbrr.separate([eng, e2], audio_il, interleaved=True)
+        t0 = time.perf_counter()
+        lbrr.separate([eng, e2], audio_il, interleaved=True, out=stems)
+        res["song_seconds"] = round(time.perf_counter() - t0, 4)
+        return res
+    finally:
+        e2.close()
 
 
 def run_song(torch, lbrr, eng, rank, world, dist, cpu_group=None):

@@ -94,9 +94,17 @@ __device__ __forceinline__ float2 twiddle(const float2* tws, int k) {
   const float2 w = tws[k & (kTwS - 1)];
   return (k & kTwS) ? make_float2(-w.x, -w.y) : w;
 }
+// 16-byte asynchronous global -> shared copies (no registers involved, all in
+// flight at once), completed by cp_async_wait_all.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
 // Copy the first kTwS entries of the global table into shared memory.
 __device__ __forceinline__ void load_twiddles(float2* tws, const float2* __restrict__ twg) {
-  for (int i = threadIdx.x; i < kTwS; i += blockDim.x) tws[i] = __ldg(twg + i);
+  for (int i = 2 * threadIdx.x; i < kTwS; i += 2 * blockDim.x) cp_async16(tws + i, twg + i);
 }
 
 // 1024-point complex FFT of one frame by one warp.  On entry lane b holds
@@ -155,10 +163,11 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
   if (interior) {
     const float4* src = reinterpret_cast<const float4*>(x + 2ll * (t * kHop - pad));
     float4* dst = reinterpret_cast<float4*>(fsm);
-    for (int i = threadIdx.x; i < kNfft / 2; i += blockDim.x) dst[i] = __ldg(src + i);
+    for (int i = threadIdx.x; i < kNfft / 2; i += blockDim.x) cp_async16(dst + i, src + i);
   }
   for (int i = threadIdx.x; i < nb * 8; i += blockDim.x) stab[i] = __ldg(tab + i);
   load_twiddles(tw, twg);
+  cp_async_wait_all();
   __syncthreads();
   if (warp < 2) {
     const int ch = warp;
@@ -281,9 +290,10 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
     shift = static_cast<int>((reinterpret_cast<uintptr_t>(X) >> 3) & 1);
     const float4* src = reinterpret_cast<const float4*>(X - shift);
     float4* dst = reinterpret_cast<float4*>(xp);
-    for (int i = lane; i < (shift + kBins + 1) / 2; i += 32) dst[i] = __ldg(src + i);
+    for (int i = lane; i < (shift + kBins + 1) / 2; i += 32) cp_async16(dst + i, src + i);
   }
   load_twiddles(tw, twg);
+  cp_async_wait_all();
   __syncthreads();
   if (has_frame) {
     const float2* X = xp + shift;
