@@ -500,15 +500,17 @@ struct Row256Maps {
 // Constants of the dense row epilogue in shared memory (EpiRow256::load_consts).
 constexpr int kRowBias = 0, kRowGamma = 256, kRowGateW = 512, kRowGateB = 512 + 2048;
 
-// kSmem: bias, gamma, gate_w and gate_b are read from the constants region
-// (x.consts, layout above) instead of global memory.
+// kSmem: bias, gamma and gate_b are read from the constants region (x.consts,
+// layout above) instead of global memory.  The gate weights always come from
+// the constants region, transposed to [256][8] by load_gate_consts, so that one
+// packed FMA updates two gates per column.
 template <bool kBandRows, bool kSmem, class RowOf>
 __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, const float* bias, const float* resid,
                                                 const Row256Maps& maps, const RowNormParams& np, int band,
                                                 RowOf row_of) {
   auto ld4 = [](const float* p) { return kSmem ? lds4(p) : ldg4(p); };
   const float* gamma = kSmem ? x.consts + kRowGamma : np.gamma;
-  const float* gate_w = kSmem ? x.consts + kRowGateW : np.gate_w;
+  const float* gate_wt = x.consts + kRowGateW;  // [256][8]: the 8 gate weights of each column together
   const float* gate_b = kSmem ? x.consts + kRowGateB : np.gate_b;
   if (kSmem) bias = x.consts + kRowBias;
   const bool valid = x.row < t.rows;
@@ -591,7 +593,9 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
   for (int p = 0; p < kParts; ++p) ss += __uint_as_float(x.quad[p * kStageWords + x.lane]);
   quad_sync(x.bar_id);
   const float scale = 16.0f / fmaxf(sqrtf(ss), 1e-12f);
-  float g[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  // gate partial sums, (gate 2i, gate 2i+1) pairs, even and odd columns apart
+  float2 ge[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+  float2 go[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
   // fp16 rows leave 64 columns at a time (32 x 64 blocks, 128-byte rows: whole
   // L2 lines); the band-major final norm scatters 32-column blocks by hand
 #pragma unroll 1
@@ -616,9 +620,14 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
         }
         if (np.norm == 2) {
 #pragma unroll
-          for (int gi = 0; gi < 8; ++gi) {
-            const float4 wg = ld4(gate_w + gi * 256 + c + 4 * j4);
-            g[gi] += h[0] * wg.x + h[1] * wg.y + h[2] * wg.z + h[3] * wg.w;
+          for (int k = 0; k < 4; ++k) {
+            const float4 wa = lds4(gate_wt + (c + 4 * j4 + k) * 8), wb = lds4(gate_wt + (c + 4 * j4 + k) * 8 + 4);
+            const float2 hh = f2(h[k], h[k]);
+            float2* acc = (k & 1) ? go : ge;
+            acc[0] = __ffma2_rn(hh, f2(wa.x, wa.y), acc[0]);
+            acc[1] = __ffma2_rn(hh, f2(wa.z, wa.w), acc[1]);
+            acc[2] = __ffma2_rn(hh, f2(wb.x, wb.y), acc[2]);
+            acc[3] = __ffma2_rn(hh, f2(wb.z, wb.w), acc[3]);
           }
         }
         w[2 * j4] = pack_f16x2(h[0], h[1]);
@@ -643,7 +652,11 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
   if (np.norm == 2) {
     x.st.drain();
 #pragma unroll
-    for (int gi = 0; gi < 8; ++gi) x.st.base[gi * 32 + x.lane] = __float_as_uint(g[gi]);
+    for (int i = 0; i < 4; ++i) {
+      const float2 gs = __fadd2_rn(ge[i], go[i]);
+      x.st.base[(2 * i) * 32 + x.lane] = __float_as_uint(gs.x);
+      x.st.base[(2 * i + 1) * 32 + x.lane] = __float_as_uint(gs.y);
+    }
     quad_sync(x.bar_id);
     if (x.part == 0 && valid) {
       float tot[8];
@@ -661,6 +674,13 @@ __device__ __forceinline__ void row256_epilogue(const TileDesc& t, EpiCtx& x, co
   }
 }
 
+// Gate weights into the constants region as [256][8] (the 8 weights of one
+// column in two 16-byte vectors), plus the 8 gate biases.
+__device__ __forceinline__ void load_gate_consts(float* c, const RowNormParams& np, int tid, int nthr) {
+  for (int i = tid; i < 2048; i += nthr) c[kRowGateW + i] = __ldg(np.gate_w + (i & 7) * 256 + (i >> 3));
+  if (tid < 8) c[kRowGateB + tid] = __ldg(np.gate_b + tid);
+}
+
 // Out-projection: attn_out = acc + bias + x, fused with the pre-FF RMSNorm
 // (matmul_resid + rmsnorm_h16, src/main.rs:6219-6234).
 // FF2: x = acc + b2 + attn_out (src/main.rs:6255-6259), fused with the next
@@ -674,10 +694,7 @@ struct EpiRow256 : DenseTiles {
   __device__ void load_consts(float* c, int tid, int nthr) const {
     copy_consts(c + kRowBias, bias, 256, tid, nthr);
     if (np.norm) copy_consts(c + kRowGamma, np.gamma, 256, tid, nthr);
-    if (np.norm == 2) {
-      copy_consts(c + kRowGateW, np.gate_w, 2048, tid, nthr);
-      if (tid < 8) c[kRowGateB + tid] = __ldg(np.gate_b + tid);
-    }
+    if (np.norm == 2) load_gate_consts(c, np, tid, nthr);
   }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     row256_epilogue<false, true>(t, x, bias, resid, maps, np, 0, [&](int r) { return t.row0 + r; });
@@ -691,6 +708,9 @@ struct EpiBand : TableTiles {
   const float* bias;  // [nb][256]
   int nb;
   RowNormParams np;
+  __device__ void load_consts(float* c, int tid, int nthr) const {
+    if (np.norm == 2) load_gate_consts(c, np, tid, nthr);
+  }
   __device__ void run(const TileDesc& t, EpiCtx& x) const {
     const int band = t.aux;
     row256_epilogue<true, false>(t, x, bias + band * 256, nullptr, maps, np, band,
