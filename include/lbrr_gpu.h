@@ -89,6 +89,13 @@ const char* lbrr_last_error(void);
 /* ABI version: 2 (2 added lbrr_chunk_plan.fade, engine options and stage entry points). */
 int lbrr_abi_version(void);
 
+/* Page-locked host memory for the host entry points (lbrr_forward_chunk_host
+ * copies straight between such buffers and the device): `bytes` of portable
+ * page-locked memory in *ptr, released by lbrr_host_free.  No counterpart in
+ * the reference, whose host buffers are ordinary Vec<f32>s staged by cudarc. */
+int lbrr_host_alloc(size_t bytes, void** ptr);
+int lbrr_host_free(void* ptr);
+
 /* Fill `desc` with the supported model (assets/logic_bs_roformer.yaml:11-84).
  * `freqs_out` receives num_bands (62) entries and is referenced by desc. */
 int lbrr_default_model(lbrr_model_desc* desc, int32_t* freqs_out, int32_t capacity);
@@ -124,10 +131,13 @@ int lbrr_check_safetensors(const char* path);
  * Replaces bench_forward + istft_ola (src/main.rs:7014-7162, :7303-7306). */
 int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);
 
-/* End to end from host memory: stage x_host through pinned memory, copy to
- * the device, forward, copy the stems back in slices (the engine's four host
- * copy threads, started by its first call of this function, move each slice
- * into stems_host as it arrives), synchronise, check the device status.
+/* End to end from host memory: copy x_host to the device, forward, copy the
+ * stems back, synchronise, check the device status.  When both buffers are
+ * page-locked (cudaHostAlloc, or cudaHostRegister over the whole range; the
+ * first and last bytes are checked), the copies go directly between them and
+ * the device.  Otherwise x_host is staged through the engine's pinned memory
+ * and the stems come back in slices that the engine's four host copy threads
+ * (started by the first such call) move into stems_host as each arrives.
  * Replaces bench_forward plus the D2H of src/main.rs:7303-7317.
  * x_host: [len][2], stems_host: [6][2][len]. */
 int lbrr_forward_chunk_host(lbrr_engine* e, const float* x_host, int64_t len, float* stems_host);

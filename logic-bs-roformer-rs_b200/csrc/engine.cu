@@ -343,6 +343,20 @@ extern "C" const char* lbrr_last_error(void) { return g_err.c_str(); }
 extern "C" int lbrr_set_error_for_host(int code, const char* msg) { return fail(code, msg ? msg : ""); }
 extern "C" int lbrr_abi_version(void) { return 2; }
 
+extern "C" int lbrr_host_alloc(size_t bytes, void** ptr) {
+  if (!ptr) return fail(LBRR_ERR_INVALID, "lbrr_host_alloc: NULL ptr");
+  *ptr = nullptr;
+  if (bytes == 0) return fail(LBRR_ERR_INVALID, "lbrr_host_alloc: zero bytes");
+  CK(cudaHostAlloc(ptr, bytes, cudaHostAllocPortable));
+  return LBRR_OK;
+}
+
+extern "C" int lbrr_host_free(void* ptr) {
+  if (!ptr) return LBRR_OK;
+  CK(cudaFreeHost(ptr));
+  return LBRR_OK;
+}
+
 extern "C" int lbrr_default_model(lbrr_model_desc* d, int32_t* freqs_out, int32_t capacity) {
   if (!d || !freqs_out || capacity < kNumBands) return fail(LBRR_ERR_INVALID, "lbrr_default_model: need 62 slots");
   for (int b = 0; b < kNumBands; ++b) freqs_out[b] = kFreqs[b];
@@ -1176,11 +1190,34 @@ extern "C" int lbrr_engine_wait_probe(lbrr_engine* e, int64_t limit_ns) {
 // memory into the caller's buffer as soon as it has arrived, so the host copy
 // overlaps the rest of the download and the last slice's copy is short.  The
 // input is staged into pinned memory by the same threads.
+// Page-locked host memory (cudaHostAlloc / cudaHostRegister): checked at the
+// first and the last byte of the range, the convention of CUDA host-copy
+// callers (a range page-locked at both ends is taken to be one allocation).
+static bool host_pinned(const void* p, size_t bytes) {
+  auto pinned = [](const void* q) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      cudaGetLastError();  // clear the sticky-free error of an unknown pointer
+      return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+  };
+  return bytes > 0 && pinned(p) && pinned(static_cast<const char*>(p) + bytes - 1);
+}
+
 extern "C" int lbrr_forward_chunk_host(lbrr_engine* e, const float* xh, int64_t len, float* outh) {
   if (int rc = check_forward_args(e, xh, len, outh)) return rc;
   DeviceGuard g(e->device);
   const size_t in_b = static_cast<size_t>(len) * 2 * sizeof(float);
   const size_t out_b = static_cast<size_t>(len) * 2 * kStems * sizeof(float);
+  if (host_pinned(xh, in_b) && host_pinned(outh, out_b)) {
+    // both buffers page-locked: the copy engines read and write them directly
+    CK(cudaMemcpyAsync(e->dev_in, xh, in_b, cudaMemcpyHostToDevice, e->stream));
+    if (int rc = lbrr_forward_chunk(e, e->dev_in, len, e->dev_out, e->stream)) return rc;
+    CK(cudaMemcpyAsync(outh, e->dev_out, out_b, cudaMemcpyDeviceToHost, e->stream));
+    CK(cudaStreamSynchronize(e->stream));
+    return check_status(e->status, e->stream);
+  }
   for (auto& ev : e->host_ev)
     if (!ev) CK(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
   const bool threaded = out_b >= (4u << 20);

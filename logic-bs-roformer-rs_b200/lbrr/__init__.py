@@ -71,6 +71,8 @@ def lib() -> C.CDLL:
     sig = {
         "lbrr_last_error": ([], C.c_char_p),
         "lbrr_abi_version": ([], C.c_int),
+        "lbrr_host_alloc": ([C.c_size_t, C.POINTER(vp)], C.c_int),
+        "lbrr_host_free": ([vp], C.c_int),
         "lbrr_default_model": ([C.POINTER(ModelDesc), C.POINTER(C.c_int32), i32], C.c_int),
         "lbrr_engine_create": ([C.c_int, C.POINTER(ModelDesc), i64, C.POINTER(vp)], C.c_int),
         "lbrr_engine_load_weights": ([vp, C.POINTER(WeightView), C.c_size_t], C.c_int),
@@ -110,7 +112,7 @@ def lib() -> C.CDLL:
 
 # Every symbol include/lbrr_gpu.h declares (checked by the CPU test suite).
 HEADER_SYMBOLS = [
-    "lbrr_last_error", "lbrr_abi_version", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
+    "lbrr_last_error", "lbrr_abi_version", "lbrr_host_alloc", "lbrr_host_free", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
     "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
     "lbrr_forward_back",
     "lbrr_engine_sync", "lbrr_engine_set_option", "lbrr_engine_get_option", "lbrr_engine_wait_probe",
@@ -270,6 +272,32 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+class _PinnedBlock:
+    """Owner of one lbrr_host_alloc block; frees it when the last array view goes."""
+
+    def __init__(self, nbytes: int):
+        p = C.c_void_p()
+        check(lib().lbrr_host_alloc(nbytes, C.byref(p)))
+        self.ptr = p.value
+
+    def __del__(self):
+        if getattr(self, "ptr", None) and _lib is not None:
+            _lib.lbrr_host_free(self.ptr)
+            self.ptr = None
+
+
+def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
+    """An uninitialised C-contiguous array in page-locked host memory
+    (lbrr_host_alloc): Engine.forward_host copies such arrays straight to and
+    from the device."""
+    dtype = np.dtype(dtype)
+    n = int(np.prod(shape)) * dtype.itemsize
+    block = _PinnedBlock(max(n, 1))
+    buf = (C.c_char * max(n, 1)).from_address(block.ptr)
+    buf._lbrr_block = block  # every numpy view holds buf, and buf holds the block
+    return np.frombuffer(buf, dtype=np.uint8, count=n).view(dtype).reshape(shape)
 
 
 def _out_array(out, shape):

@@ -120,3 +120,21 @@ def test_song_demix_matches_oracle_plan(engine):
     ref = R.demix(model, audio)
     # same fp32 products, sums and divisions in the same chunk order: bit-equal
     assert np.array_equal(got, ref), snr_db(got, ref)
+
+
+def test_host_entry_page_locked_matches_pageable(engine):
+    """lbrr_forward_chunk_host copies page-locked buffers (lbrr_host_alloc)
+    straight to and from the device and stages ordinary ones; both give the
+    same bits, including a mixed call (page-locked input, pageable output)."""
+    import lbrr
+    audio = R.synth_audio(SHORT, seed=22)
+    xp = interleave(audio)
+    ref = engine.forward_host(xp)
+    xh = lbrr.pinned_empty(xp.shape)
+    xh[:] = xp
+    yh = lbrr.pinned_empty(ref.shape)
+    yh[:] = np.nan
+    engine.forward_host(xh, out=yh)
+    assert np.array_equal(yh, ref)
+    mixed = engine.forward_host(xh)
+    assert np.array_equal(mixed, ref)
