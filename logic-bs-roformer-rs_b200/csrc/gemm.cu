@@ -309,16 +309,19 @@ struct EpiQKV : DenseTiles {
   const float* sin;
   int nb, axis;
   // constants: bias [0, 1536); RoPE rows from kRope as [pos][cos 32 | sin 32]:
-  // frequency axis the whole table (nb <= kMaxNb positions), time axis a
+  // frequency axis the whole table (nb <= kMaxNb positions, rows kRopeStride
+  // floats apart so that the 32 lanes of a warp, 32 different band positions,
+  // spread their 16-byte reads over all 32 banks), time axis a
   // per-warp cache of the (at most two) frames its 32 rows fall in
   static constexpr int kRope = 1536;
-  static constexpr int kMaxNb = (kConstFloats - kRope) / 64;
+  static constexpr int kRopeStride = 68;
+  static constexpr int kMaxNb = (kConstFloats - kRope) / kRopeStride;
   __device__ void load_consts(float* c, int tid, int nthr) const {
     copy_consts(c, bias16, 1536, tid, nthr);
     if (axis == 1 && nb <= kMaxNb)
       for (int i = tid; i < nb * 64; i += nthr) {
         const int pos = i >> 6, k = i & 63;
-        c[kRope + i] = k < 32 ? __ldg(cos + pos * 32 + k) : __ldg(sin + pos * 32 + k - 32);
+        c[kRope + pos * kRopeStride + k] = k < 32 ? __ldg(cos + pos * 32 + k) : __ldg(sin + pos * 32 + k - 32);
       }
   }
   FastDiv nbd;  // division by nb
@@ -379,7 +382,7 @@ struct EpiQKV : DenseTiles {
     bool rope_smem = false;
     if (axis == 1) {
       if (nb <= kMaxNb) {
-        rope = x.consts + kRope + pos * 64;
+        rope = x.consts + kRope + pos * kRopeStride;
         rope_smem = true;
       }
     } else {
