@@ -170,7 +170,8 @@ def time_dominant_kernel(torch, lbrr, T=1151, iters=10):
 
 def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
     """per-kernel tensor throughput at M = 62*T of the trunk
-    GEMMs -- QKV (+bias+RoPE), out-projection (+residual+norm), FF1 (+GELU),
+    GEMMs -- QKV (+bias+RoPE at the frame on the time axis, at the band on the
+    frequency axis), out-projection (+residual+norm), FF1 (+GELU),
     FF2 (+residual) -- and the fused feed-forward the forward actually runs."""
     M = T * 62
     g = torch.Generator(device="cuda").manual_seed(1)
@@ -179,6 +180,8 @@ def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
     b16 = torch.zeros(1536, device="cuda")
     cos = torch.ones(T, 32, device="cuda")
     sin = torch.zeros(T, 32, device="cuda")
+    cos_f = torch.ones(62, 32, device="cuda")
+    sin_f = torch.zeros(62, 32, device="cuda")
     qkv = torch.empty(M, 1536, device="cuda", dtype=torch.float16)
     sc = torch.randn(M, 512, device="cuda", generator=g).half()
     wo = (torch.randn(256, 512, device="cuda", generator=g) * 0.02).half()
@@ -194,6 +197,7 @@ def time_trunk_gemms(torch, lbrr, T=1151, iters=10):
     f1 = torch.empty(M, 1024, device="cuda", dtype=torch.float16)
     cases = {
         "qkv": (lambda s: lbrr.qkv_rope(h, w_qkv, b16, cos, sin, qkv, T, 62, 0, stream=s), 2 * M * 1536 * 256),
+        "qkv_freq": (lambda s: lbrr.qkv_rope(h, w_qkv, b16, cos_f, sin_f, qkv, T, 62, 1, stream=s), 2 * M * 1536 * 256),
         "out_proj": (lambda s: lbrr.outproj_norm(sc, wo, bo, x, gam, ao, h2, stream=s), 2 * M * 256 * 512),
         "ff1_gelu": (lambda s: lbrr.ff1_gelu(h, w1, b1, f1, stream=s), 2 * M * 1024 * 256),
         "ff2_resid": (lambda s: lbrr.ff2_resid(f1, w2, bo, x, xo, stream=s), 2 * M * 256 * 1024),
