@@ -346,8 +346,9 @@ __global__ void __launch_bounds__(kT1Threads, 2)
 // one-item CTA; here each CTA (two per SM) walks items with a stride of the
 // grid and a 2-stage TMA ring: item k+1's Q/K/V arrive while item k runs.
 // TMEM (256 columns): S 0..127, O 128..191, P 192..255.  Warp 0 loads, warp 1
-// issues S = Q K^T once the previous item's output has left TMEM and O = P V
-// once P is written, warps 2..5 run the softmax (one row per thread, only the
+// issues S = Q K^T as soon as the previous item's P is written (so it runs
+// during that item's epilogue) and O = P V once P is written and the previous
+// output has left TMEM, warps 2..5 run the softmax (one row per thread, only the
 // row's own sequence as keys) and the epilogue f16(f16(O/l) * sigmoid(gate)).
 constexpr int kFStages = 2;
 constexpr int kFStage = 3 * kTile;  // Q, K, V
@@ -430,9 +431,11 @@ __global__ void __launch_bounds__(kFThreads, 2)
       for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++k) {
         const int st = k & 1;
         const uint32_t sq = smem_u32(smem + st * kFStage), sk = sq + kTile, sv = sq + 2 * kTile;
+        // S is free: the previous item's softmax read it before P was written,
+        // and P was waited for before that item's P.V was issued.  S is
+        // computed while the softmax warps run the previous item's epilogue;
+        // its commit also covers the previous P.V, so P may be rewritten.
         ok = mbar_wait(&full[st], (k >> 1) & 1, abort_flag, a.status);
-        // the previous item's softmax and epilogue are done with S, P and O
-        if (ok && k > 0) ok = mbar_wait(tmem_free, (k - 1) & 1, abort_flag, a.status);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
@@ -441,6 +444,8 @@ __global__ void __launch_bounds__(kFThreads, 2)
                      kk > 0 ? 1u : 0u);
         mma_commit(s_full);
         ok = mbar_wait(p_full, k & 1, abort_flag, a.status);
+        // the previous item's epilogue is done with O
+        if (ok && k > 0) ok = mbar_wait(tmem_free, (k - 1) & 1, abort_flag, a.status);
         if (!ok) break;
         tc_fence_after();
 #pragma unroll
