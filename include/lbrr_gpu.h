@@ -135,7 +135,9 @@ int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* s
  * stems back, synchronise, check the device status.  When both buffers are
  * page-locked (cudaHostAlloc, or cudaHostRegister over the whole range; the
  * first and last bytes are checked), the copies go directly between them and
- * the device.  Otherwise x_host is staged through the engine's pinned memory
+ * the device, and each stem's download starts as soon as that stem's mask
+ * and inverse transform are done, while the next stem is computed.
+ * Otherwise x_host is staged through the engine's pinned memory
  * and the stems come back in slices that the engine's four host copy threads
  * (started by the first such call) move into stems_host as each arrives.
  * Replaces bench_forward plus the D2H of src/main.rs:7303-7317.
