@@ -1630,6 +1630,9 @@ struct SongRun {
   std::vector<cudaEvent_t> strip_ev;  // created on the producing engine's device
   std::vector<int> rc;
   std::vector<std::string> msg;
+  // caller buffers that are page-locked: interior chunks are uploaded from the
+  // song itself, finished regions are downloaded straight into the output
+  bool direct_in = false, direct_out = false;
 };
 
 // The Hann fade table on engine e's device (current device), uploaded once per chunk length.
@@ -1710,29 +1713,36 @@ void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, fl
     const int slot = k & 1;
     const int64_t s = starts[c];
     // chunk input: padded samples [s, s + C), reflected outside the song
-    if (cudaEventSynchronize(e->song_ev_in[slot]) != cudaSuccess) return bail(fail(LBRR_ERR_CUDA, "input slot"));
-    float* pin = e->song_pin_in[slot];
     const int64_t lo = std::max<int64_t>(s, g.border), hi = std::min<int64_t>(s + g.C, g.border + g.len);
-    if (hi > lo) std::memcpy(pin + 2 * (lo - s), xh + 2 * (lo - g.border), static_cast<size_t>(hi - lo) * 2 * sizeof(float));
-    for (int64_t p = s; p < s + g.C; ++p) {
-      if (p >= lo && p < hi) {
-        p = hi - 1;
-        continue;
+    if (run.direct_in && lo == s && hi == s + g.C) {
+      // wholly inside a page-locked song: one DMA, no staging
+      if (cudaMemcpyAsync(e->dev_in, xh + 2 * (s - g.border), static_cast<size_t>(g.C) * 2 * sizeof(float),
+                          cudaMemcpyHostToDevice, e->stream) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "chunk upload"));
+    } else {
+      if (cudaEventSynchronize(e->song_ev_in[slot]) != cudaSuccess) return bail(fail(LBRR_ERR_CUDA, "input slot"));
+      float* pin = e->song_pin_in[slot];
+      if (hi > lo) std::memcpy(pin + 2 * (lo - s), xh + 2 * (lo - g.border), static_cast<size_t>(hi - lo) * 2 * sizeof(float));
+      for (int64_t p = s; p < s + g.C; ++p) {
+        if (p >= lo && p < hi) {
+          p = hi - 1;
+          continue;
+        }
+        int64_t src = 0;
+        if (g.len > 1) {
+          const int64_t period = 2 * (g.len - 1);
+          int64_t q = (p - g.border) % period;
+          if (q < 0) q += period;
+          src = q < g.len ? q : period - q;
+        }
+        pin[2 * (p - s)] = xh[2 * src];
+        pin[2 * (p - s) + 1] = xh[2 * src + 1];
       }
-      int64_t src = 0;
-      if (g.len > 1) {
-        const int64_t period = 2 * (g.len - 1);
-        int64_t q = (p - g.border) % period;
-        if (q < 0) q += period;
-        src = q < g.len ? q : period - q;
-      }
-      pin[2 * (p - s)] = xh[2 * src];
-      pin[2 * (p - s) + 1] = xh[2 * src + 1];
+      if (cudaMemcpyAsync(e->dev_in, pin, static_cast<size_t>(g.C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
+                          e->stream) != cudaSuccess ||
+          cudaEventRecord(e->song_ev_in[slot], e->stream) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "chunk upload"));
     }
-    if (cudaMemcpyAsync(e->dev_in, pin, static_cast<size_t>(g.C) * 2 * sizeof(float), cudaMemcpyHostToDevice,
-                        e->stream) != cudaSuccess ||
-        cudaEventRecord(e->song_ev_in[slot], e->stream) != cudaSuccess)
-      return bail(fail(LBRR_ERR_CUDA, "chunk upload"));
     if (e->song_fail_chunk == c)  // host-side failure injection (tests of the abort path)
       return bail(fail(LBRR_ERR_STATE, "injected failure before the forward of chunk " + std::to_string(c)));
     if (int rc = lbrr_forward_chunk(e, e->dev_in, g.C, e->dev_out, e->stream)) return bail(rc);
@@ -1779,7 +1789,17 @@ void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, fl
     }
     // the host copy of the previous region overlaps this chunk's GPU work
     if (int rc = scatter()) return bail(rc);
-    if (nreg > 0) {
+    if (nreg > 0 && run.direct_out) {
+      // page-locked output: the 12 channel rows of the region go straight to
+      // their places in the caller's planar array (one 2-D copy)
+      if (cudaEventRecord(e->song_ev_reg[slot], e->stream) != cudaSuccess ||
+          cudaStreamWaitEvent(e->song_copy, e->song_ev_reg[slot], 0) != cudaSuccess ||
+          cudaMemcpy2DAsync(outh + o0, static_cast<size_t>(g.len) * sizeof(float), e->song_fin[slot],
+                            static_cast<size_t>(nreg) * sizeof(float), static_cast<size_t>(nreg) * sizeof(float),
+                            2 * kStems, cudaMemcpyDeviceToHost, e->song_copy) != cudaSuccess ||
+          cudaEventRecord(e->song_ev_out[slot], e->song_copy) != cudaSuccess)
+        return bail(fail(LBRR_ERR_CUDA, "region download"));
+    } else if (nreg > 0) {
       // the download runs on the copy stream, so the next chunk's forward on
       // the compute stream does not wait for it
       if (cudaEventRecord(e->song_ev_reg[slot], e->stream) != cudaSuccess ||
@@ -1795,6 +1815,8 @@ void song_worker(lbrr_engine* const* engines, int n, int me, const float* xh, fl
     }
   }
   if (int rc = scatter()) return bail(rc);
+  if (run.direct_out && cudaStreamSynchronize(e->song_copy) != cudaSuccess)
+    return bail(fail(LBRR_ERR_CUDA, "region download"));
   if (int rc = check_status(e->status, e->stream)) return bail(rc);
 }
 }  // namespace
@@ -1836,6 +1858,8 @@ extern "C" int lbrr_separate_song(lbrr_engine* const* engines, int n, const floa
     g.hann = engines[0]->song_hann;  // non-null marks the Hann plan; each worker uses its own copy
   }
   SongRun run;
+  run.direct_in = host_pinned(xh, static_cast<size_t>(len) * 2 * sizeof(float));
+  run.direct_out = host_pinned(outh, static_cast<size_t>(len) * 2 * kStems * sizeof(float));
   run.strip_ready.assign(g.nc, 0);
   run.strip_ev.assign(g.nc, nullptr);
   run.rc.assign(workers, LBRR_OK);

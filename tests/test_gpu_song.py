@@ -112,3 +112,31 @@ def test_two_gpus_match_one(weights):
     finally:
         e1.close()
         e0.close()
+
+
+def test_page_locked_song_buffers_same_bits(weights):
+    """With a page-locked song and output array (lbrr.pinned_empty) interior
+    chunks are uploaded straight from the song and finished regions are
+    downloaded straight into the output; the bits are those of the staged path,
+    for both plans and a song whose chunks include reflected edges."""
+    import lbrr
+    e0, e1 = _engine(0, weights), _engine(0, weights)
+    try:
+        audio = R.synth_audio(3 * R.CHUNK + 4321, seed=23)
+        il = np.ascontiguousarray(audio.T)
+        xh = lbrr.pinned_empty(il.shape)
+        xh[:] = il
+        for plan in ({}, lbrr.HANN50):
+            ref = lbrr.separate([e0, e1], il, interleaved=True, **plan)
+            out = lbrr.pinned_empty(ref.shape)
+            out[:] = np.nan
+            lbrr.separate([e0, e1], xh, interleaved=True, out=out, **plan)
+            assert np.array_equal(out, ref)
+            # pinned input with a pageable output, and the reverse
+            assert np.array_equal(lbrr.separate([e0, e1], xh, interleaved=True, **plan), ref)
+            out[:] = np.nan
+            lbrr.separate([e0, e1], il, interleaved=True, out=out, **plan)
+            assert np.array_equal(out, ref)
+    finally:
+        e1.close()
+        e0.close()
