@@ -237,7 +237,11 @@ void lbrr_engine_destroy(lbrr_engine* e);
  * over NVLink between GPUs), and copies them to host_out itself; the result
  * is bit-identical to accumulating all chunks in order on one GPU, whatever
  * n_engines is.  Plans overlapping by half or more accumulate on engines[0].
- * host_interleaved: [len][2]; host_out: [6][2][len]. */
+ * host_interleaved: [len][2]; host_out: [6][2][len].  Either buffer may be
+ * page-locked (lbrr_host_alloc, or any cudaHostAlloc / cudaHostRegister
+ * range covering it): the engines then copy chunks in and finished regions
+ * out by DMA straight from and into it instead of through their own pinned
+ * staging buffers; the result is the same bits. */
 int lbrr_separate_song(lbrr_engine* const* engines, int n_engines, const float* host_interleaved, int64_t len,
                        const lbrr_chunk_plan* plan, float* host_out);
 

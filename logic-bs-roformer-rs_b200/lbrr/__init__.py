@@ -313,7 +313,8 @@ def separate(engines, audio: np.ndarray, chunk=CHUNK, step=STEP, border=BORDER, 
     """Whole-song demix over one or more engines (separate(), src/main.rs:7598-7819).
     audio: planar [2][len] fp32, or interleaved [len][2] (the WAV layout the C
     ABI takes, passed without a copy) with interleaved=True -> stems
-    [6][2][len] fp32, written into `out` when given."""
+    [6][2][len] fp32, written into `out` when given.  Arrays from
+    pinned_empty() move by DMA without host staging copies (same bits)."""
     if interleaved:
         x = np.ascontiguousarray(audio, dtype=np.float32)
         if x.ndim != 2 or x.shape[1] != 2:
