@@ -327,6 +327,7 @@ def run_ours(args, rank, world, local_rank):
             g["pct_of_peak"] = round(100.0 * g["tflops"] / pk["tflops"], 1)
         mask = time_mask_estimator(torch, eng, x, out, stream, flush, args)
         dual = time_two_in_flight(torch, lbrr, eng, x, out, local_rank, args)
+        batched = time_batched_chunks(torch, lbrr, local_rank, stream, flush, args)
         short = time_short_chunk(torch, eng, stream, flush, args)
         wb, sb = eng.memory()
         result = {
@@ -355,6 +356,7 @@ def run_ours(args, rank, world, local_rank):
             "short_chunk": short,
             "mask_estimator": mask,
             "two_in_flight": dual,
+            "batched_chunks": batched,
             "chunk_rtf": round(ms / (CHUNK / SR * 1000.0), 6),
             "song": song,
             "clocks": clocks,
@@ -409,6 +411,26 @@ def time_short_chunk(torch, eng, stream, flush, args):
     eng.sync()
     return {"ms": round(ms, 4), "tflops": round(SHORT_FLOP / ms / 1e9, 1), "samples": L, "frames": 259,
             "published_rtx3080_ms": 33.81}
+
+
+def time_batched_chunks(torch, lbrr, local_rank, stream, flush, args):
+    """Multi-chunk batching: two full chunks in one forward (lbrr_forward_chunks
+    on an engine with room for 2 x 1151 frames), CUDA events per batch with L2
+    flushed between batches; ms per chunk = batch time / 2."""
+    from lbrr import synthetic
+    eb = lbrr.Engine(local_rank, 2 * CHUNK + 512)
+    try:
+        eb.upload_weights(synthetic.checkpoint(seed=0))
+        x2 = torch.from_numpy(np.stack([np.ascontiguousarray(synthetic.audio(CHUNK, seed=s).T)
+                                        for s in (1, 2)])).cuda()
+        out2 = torch.empty(2, 6, 2, CHUNK, device="cuda")
+        ms = _time_steps(torch, lambda: eb.forward_chunks(x2, out2, stream=stream), stream, flush,
+                         min(args.steps, 10), 3)
+        eb.sync()
+        return {"ms_per_chunk": round(ms / 2, 4), "ms_per_batch": round(ms, 4), "chunks": 2,
+                "how": "lbrr_forward_chunks: both chunks' frames in every launch (2 x 1151 frames), graph replay"}
+    finally:
+        eb.close()
 
 
 def time_two_in_flight(torch, lbrr, eng, x, out, local_rank, args):

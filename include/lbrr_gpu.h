@@ -131,6 +131,20 @@ int lbrr_check_safetensors(const char* path);
  * Replaces bench_forward + istft_ola (src/main.rs:7014-7162, :7303-7306). */
 int lbrr_forward_chunk(lbrr_engine* e, const float* x_dev, int64_t len, float* stems_dev, void* stream);
 
+/* Multi-chunk batching (the bench_forward pass of src/main.rs:7014-7162 over
+ * n_chunks chunks of the same len at once): x_dev: n_chunks x [len][2] fp32
+ * one after another, stems_dev: n_chunks x [6][2][len] fp32.  Every stage
+ * runs once over the frames of all chunks (the GEMMs, the mask estimator and
+ * the frequency-axis attention see n_chunks * T frames; the time-axis
+ * attention and its RoPE keep each chunk's frames apart), so each chunk's
+ * stems are bit-identical to lbrr_forward_chunk on that chunk alone.  Needs
+ * n_chunks * (len / 512 + 1) <= max_chunk_samples / 512 + 1 (an engine made
+ * with max_chunk_samples >= n_chunks * len + (n_chunks - 1) * 512).  With
+ * LBRR_OPT_FFT_BACKEND 1 or LBRR_OPT_DC_NYQUIST_IMAG set the chunks run one
+ * forward each.  Replayed as a CUDA graph like lbrr_forward_chunk. */
+int lbrr_forward_chunks(lbrr_engine* e, const float* x_dev, int64_t len, int32_t n_chunks, float* stems_dev,
+                        void* stream);
+
 /* End to end from host memory: copy x_host to the device, forward, copy the
  * stems back, synchronise, check the device status.  When both buffers are
  * page-locked (cudaHostAlloc, or cudaHostRegister over the whole range; the

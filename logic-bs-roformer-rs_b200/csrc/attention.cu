@@ -57,6 +57,9 @@ __device__ __forceinline__ float ex2(float x) {
 // columns, right after O += P(j)·V(j) (TS form, A = P from TMEM).  The
 // softmax warpgroup takes 224 registers per thread from warpgroup 1
 // (setmaxnreg), enough for a whole S row and its fp16 P without spilling.
+// Chunks batched into one forward are grid.z: chunk c's frames are rows
+// c*T.. of the frame axis; the key rows past its T valid frames (the next
+// chunk's, or the tensor map's zero fill after the last chunk) are masked.
 constexpr int kT1Threads = 256;
 constexpr int kT1WarpTma = 4, kT1WarpMma = 5;
 constexpr int kT1RegsSoftmax = 224, kT1RegsOther = 32;
@@ -94,6 +97,7 @@ __global__ void __launch_bounds__(kT1Threads, 2)
   const int nb = a.nb, T = a.T, nk = a.nk;
   const int head = blockIdx.y & 7, band = blockIdx.y >> 3;
   const int qt = blockIdx.x;
+  const int t0 = blockIdx.z * T;  // this chunk's first frame
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -126,14 +130,14 @@ __global__ void __launch_bounds__(kT1Threads, 2)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_3d(smem + kT1OffQ, &tm, q_full, head * 64, band, qt * 128);
+      tma_load_3d(smem + kT1OffQ, &tm, q_full, head * 64, band, t0 + qt * 128);
       for (int j = 0; j < nk; ++j) {
         const int st = j % kT1Stages;
         if (!mbar_wait(&kv_empty[st], ((j / kT1Stages) & 1) ^ 1u, abort_flag, a.status)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
         uint8_t* kv = smem + kT1OffKV + st * 2 * kTile;
-        tma_load_3d(kv, &tm, &kv_full[st], 512 + head * 64, band, j * 128);
-        tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, j * 128);
+        tma_load_3d(kv, &tm, &kv_full[st], 512 + head * 64, band, t0 + j * 128);
+        tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, t0 + j * 128);
       }
     }
   } else if (warp == kT1WarpMma) {
@@ -200,7 +204,7 @@ __global__ void __launch_bounds__(kT1Threads, 2)
     const uint32_t tP = tmem + lane_off + kColP;
     const int qi = qt * 128 + r;
     const bool valid = qi < T;
-    const int token = qi * nb + band;
+    const int token = (t0 + qi) * nb + band;
     // the gate is needed only in the epilogue; its load latency hides here
     const float gate = valid ? __ldg(a.gates + static_cast<size_t>(token) * 8 + head) : 0.f;
     const float sc = 0.125f * 1.4426950408889634f;  // SDPA scale 64^-1/2, in log2 units
@@ -554,8 +558,8 @@ __global__ void __launch_bounds__(kFThreads, 2)
 }
 }  // namespace
 
-cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
-                          cudaStream_t st) {
+cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int chunks,
+                          int* status, cudaStream_t st) {
   static unsigned long long configured = 0;
   cudaError_t ce = once_per_device(configured, [] {
     cudaError_t e = cudaFuncSetAttribute(attn_freq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kFSmem);
@@ -573,6 +577,8 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   if (ce != cudaSuccess) return ce;
   if (T <= 0) return cudaSuccess;
   if (axis == 1 && nb > 64) return cudaErrorInvalidValue;  // two sequences of <= 64 tokens per 128-row tile
+  if (chunks < 1 || chunks > 65535 || static_cast<int64_t>(T) * chunks > (1 << 30) / nb)
+    return cudaErrorInvalidValue;
   CUtensorMap tm;
   cudaError_t e;
   AttnArgs a;
@@ -583,14 +589,18 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   a.axis = axis;
   a.status = status;
   if (axis == 0) {
-    e = make_map_3d(&tm, qkv, 1536, nb, T, 1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
+    e = make_map_3d(&tm, qkv, 1536, nb, static_cast<uint64_t>(T) * chunks, 1536 * 2,
+                    static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
     if (e != cudaSuccess) return e;
     a.nk = (T + 127) / 128;
     // one query tile per CTA, two CTAs per SM
     count_launch();
-    attn_time_kernel<<<dim3(a.nk, nb * 8), kT1Threads, kT1Smem, st>>>(tm, a);
+    attn_time_kernel<<<dim3(a.nk, nb * 8, chunks), kT1Threads, kT1Smem, st>>>(tm, a);
     return cudaGetLastError();
   }
+  // frequency axis: every frame of every chunk is one sequence
+  T *= chunks;
+  a.T = T;
   // boxes of one frame's nb tokens
   e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, nb);
   if (e != cudaSuccess) return e;

@@ -239,7 +239,8 @@ struct lbrr_engine {
   int *band_f0 = nullptr, *band_d = nullptr, *band_o2 = nullptr;
   // per-length state
   int64_t cur_len = -1;
-  int cur_T = -1;
+  int cur_T = -1;  // frames of one chunk
+  int cur_B = 1;   // chunks batched along the frame axis (lbrr_forward_chunks)
   float *cos_t = nullptr, *sin_t = nullptr, *cos_f = nullptr, *sin_f = nullptr;
   TileDesc *tiles_band = nullptr, *tiles_m1 = nullptr, *tiles_m2 = nullptr;
   int n_band = 0, n_m1 = 0, n_m2 = 0;
@@ -282,6 +283,7 @@ struct lbrr_engine {
   const float* graph_x = nullptr;
   float* graph_out = nullptr;
   int64_t graph_len = -1;
+  int graph_B = 0;
   cudaStream_t graph_stream = nullptr;
   int graph_seen = 0;
   // lbrr_forward_chunk_host with page-locked buffers: the forward up to the
@@ -786,19 +788,28 @@ static void drop_graph(lbrr_engine* e) {
   e->head_len = -1;
 }
 
-static int setup_length_impl(lbrr_engine* e, int64_t len);
-static int setup_length(lbrr_engine* e, int64_t len) {
-  if (e->cur_len == len) return LBRR_OK;
+// Frames of all chunks of the current forward (the row count of every
+// frame-major buffer).
+static int frames_all(const lbrr_engine* e) { return e->cur_T * e->cur_B; }
+
+static int setup_length_impl(lbrr_engine* e, int64_t len, int B);
+static int setup_length(lbrr_engine* e, int64_t len, int B = 1) {
+  if (e->cur_len == len && e->cur_B == B) return LBRR_OK;
   const auto t0 = std::chrono::steady_clock::now();
-  const int rc = setup_length_impl(e, len);
+  const int rc = setup_length_impl(e, len, B);
   e->us_setup = us_since(t0);
   return rc;
 }
 
-static int setup_length_impl(lbrr_engine* e, int64_t len) {
+// Per-length tables for B chunks of len samples batched along the frame axis
+// (B * T frames): the time-axis RoPE table repeats its T positions for every
+// chunk, the grouped GEMMs' tile tables run over all B * T frames, the ISTFT
+// envelope and the FFT plans are those of one chunk.
+static int setup_length_impl(lbrr_engine* e, int64_t len, int B) {
   drop_graph(e);  // it refers to the per-length buffers released below
   const BandGeom& G = geom();
-  const int T = T_of(len);
+  const int T1 = T_of(len);
+  const int T = T1 * B;  // frames of all chunks
   const int mt = (T + 127) / 128;
   // RoPE tables (time: T positions, freq: 62) -- one allocation for the tables,
   // tile tables follow in a second allocation, both released on the next change
@@ -811,7 +822,14 @@ static int setup_length_impl(lbrr_engine* e, int64_t len) {
   e->tiles_band = nullptr;
   e->inv_env = nullptr;
   std::vector<float> ct, st, cf, sf;
-  rope_table(T, ct, st);
+  {
+    std::vector<float> c1, s1;
+    rope_table(T1, c1, s1);
+    for (int b = 0; b < B; ++b) {
+      ct.insert(ct.end(), c1.begin(), c1.end());
+      st.insert(st.end(), s1.begin(), s1.end());
+    }
+  }
   rope_table(kNumBands, cf, sf);
   float* tabs = nullptr;
   CK(cudaMalloc(&tabs, (2 * ct.size() + 2 * cf.size()) * sizeof(float)));
@@ -860,7 +878,7 @@ static int setup_length_impl(lbrr_engine* e, int64_t len) {
   {
     std::vector<float> win(kNfft), env(static_cast<size_t>(len) + kNfft, 0.f);
     for (int i = 0; i < kNfft; ++i) win[i] = static_cast<float>(0.5 * (1.0 - std::cos(2.0 * M_PI * i / kNfft)));
-    for (int t = 0; t < T; ++t)
+    for (int t = 0; t < T1; ++t)
       for (int nn = 0; nn < kNfft; ++nn) {
         const size_t p = static_cast<size_t>(t) * kHop + nn;
         if (p < env.size()) env[p] += win[nn] * win[nn];
@@ -877,7 +895,7 @@ static int setup_length_impl(lbrr_engine* e, int64_t len) {
     cufftDestroy(e->plan_c2r);
     e->plans = false;
   }
-  if (need_cufft && (e->cur_T != T || !e->plans)) {
+  if (need_cufft && (e->cur_T != T1 || !e->plans)) {
     if (e->plans) {
       cufftDestroy(e->plan_r2c);
       cufftDestroy(e->plan_c2r);
@@ -885,11 +903,12 @@ static int setup_length_impl(lbrr_engine* e, int64_t len) {
     }
     int n[1] = {kNfft};
     int inr[1] = {kNfft}, outc[1] = {kBins};
-    CKFFT(cufftPlanMany(&e->plan_r2c, 1, n, inr, 1, kNfft, outc, 1, kBins, CUFFT_R2C, 2 * T));
-    CKFFT(cufftPlanMany(&e->plan_c2r, 1, n, outc, 1, kBins, inr, 1, kNfft, CUFFT_C2R, 2 * kStems * T));
+    CKFFT(cufftPlanMany(&e->plan_r2c, 1, n, inr, 1, kNfft, outc, 1, kBins, CUFFT_R2C, 2 * T1));
+    CKFFT(cufftPlanMany(&e->plan_c2r, 1, n, outc, 1, kBins, inr, 1, kNfft, CUFFT_C2R, 2 * kStems * T1));
     e->plans = true;
   }
-  e->cur_T = T;
+  e->cur_T = T1;
+  e->cur_B = B;
   e->cur_len = len;
   return LBRR_OK;
 }
@@ -920,8 +939,9 @@ static bool use_cufft_back(const lbrr_engine* e) { return e->fft_backend == 1 ||
 
 static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t st) {
   const BandGeom& G = geom();
-  const int T = e->cur_T;
+  const int T = e->cur_T, Tall = frames_all(e);
   if (use_cufft_front(e)) {
+    if (e->cur_B != 1) return fail(LBRR_ERR_STATE, "batched chunks need the in-house FFT");
     CKL(stft_frames(x, e->window, e->frames, static_cast<int>(len), T, st));
     CKFFT(cufftSetStream(e->plan_r2c, st));
     CKFFT(cufftExecR2C(e->plan_r2c, e->frames, reinterpret_cast<cufftComplex*>(e->spec)));
@@ -929,10 +949,10 @@ static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t s
   } else {
     // framing + FFT + spectrum + band RMSNorm in one kernel
     CKL(stft_front(x, e->window, e->twiddles, e->spec, e->band_g, e->band_tab, e->xn, G.xn_cols,
-                   static_cast<int>(len), T, kNumBands, st));
+                   static_cast<int>(len), T, kNumBands, e->cur_B, st));
   }
   // band split, fused with step 0's pre-attention RMSNorm + gates
-  CKL(gemm_bandsplit(e->xn, G.xn_cols, e->band_w, G.kpad_max, e->band_b, e->x, T, kNumBands, e->tiles_band,
+  CKL(gemm_bandsplit(e->xn, G.xn_cols, e->band_w, G.kpad_max, e->band_b, e->x, Tall, kNumBands, e->tiles_band,
                      e->n_band, attn_norm(e, 0), e->status, st));
   return LBRR_OK;
 }
@@ -941,11 +961,11 @@ static int run_front(lbrr_engine* e, const float* x, int64_t len, cudaStream_t s
 // the previous step's FF2); after the last step that epilogue writes the final
 // norm in band-major order instead.
 static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
-  const int T = e->cur_T, M = T * kNumBands, axis = k & 1;
+  const int T = e->cur_T, Tall = frames_all(e), M = Tall * kNumBands, axis = k & 1;
   const StepWeights& w = e->steps[k];
   CKL(gemm_qkv(e->h16, w.wqkv, e->qkv_bias16, axis == 0 ? e->cos_t : e->cos_f, axis == 0 ? e->sin_t : e->sin_f,
                e->qkv, M, kNumBands, axis, e->status, st));
-  CKL(attention_fwd(e->qkv, e->gates, e->scaled, T, kNumBands, axis, e->status, st));
+  CKL(attention_fwd(e->qkv, e->gates, e->scaled, T, kNumBands, axis, e->cur_B, e->status, st));
   CKL(gemm_outproj_norm(e->scaled, w.wo, e->out_bias, e->x, w.ff_g, e->attn_out, e->h16, M, e->status, st));
   RowNorm next;
   if (k + 1 < 2 * kDepth) {
@@ -954,7 +974,7 @@ static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
     next.kind = 3;
     next.gamma = e->final_g;
     next.xb16 = e->xb16;
-    next.T = T;
+    next.T = Tall;
     next.nb = kNumBands;
   }
   // FF1 -> GELU -> FF2 + residual, the hidden activation kept on chip
@@ -964,19 +984,21 @@ static int run_step(lbrr_engine* e, int k, cudaStream_t st) {
 
 static int run_back(lbrr_engine* e, int64_t len, float* out, cudaStream_t st) {
   const BandGeom& G = geom();
-  const int T = e->cur_T;
-  CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, T, kStems * kNumBands, e->tiles_m1, e->n_m1, e->status,
-                 st));
-  CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
+  const int T = e->cur_T, Tall = frames_all(e);
+  CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, Tall, kStems * kNumBands, e->tiles_m1, e->n_m1,
+                 e->status, st));
+  CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, Tall, kStems,
                  G.n2tot, e->tiles_m2, e->n_m2, e->keep_dc_imag, e->status, st));
   if (use_cufft_back(e)) {
+    if (e->cur_B != 1) return fail(LBRR_ERR_STATE, "batched chunks need the in-house FFT");
     CKFFT(cufftSetStream(e->plan_c2r, st));
     CKFFT(cufftExecC2R(e->plan_c2r, reinterpret_cast<cufftComplex*>(e->c2r), e->pcm));
     CKL(istft_ola(e->pcm, e->window, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
     e->pcm_valid = true;
   } else {
     // inverse FFT + window + overlap-add + envelope in one kernel
-    CKL(istft_back(e->c2r, e->window, e->twiddles, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, st));
+    CKL(istft_back(e->c2r, e->window, e->twiddles, e->inv_env, out, static_cast<int>(len), T, 2 * kStems, e->cur_B,
+                   st));
     e->pcm_valid = false;
   }
   return LBRR_OK;
@@ -1007,8 +1029,8 @@ static int run_head(lbrr_engine* e, int64_t len, cudaStream_t st) {
   if (int rc = run_front(e, e->dev_in, len, st)) return rc;
   for (int k = 0; k < 2 * kDepth; ++k)
     if (int rc = run_step(e, k, st)) return rc;
-  CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, e->cur_T, kStems * kNumBands, e->tiles_m1, e->n_m1,
-                 e->status, st));
+  CKL(gemm_mask1(e->xb16, e->mask_w1, e->mask_b1, e->hidden, frames_all(e), kStems * kNumBands, e->tiles_m1,
+                 e->n_m1, e->status, st));
   return LBRR_OK;
 }
 
@@ -1019,13 +1041,14 @@ static int run_head(lbrr_engine* e, int64_t len, cudaStream_t st) {
 static int run_tail_per_stem(lbrr_engine* e, int64_t len, float* outh, cudaStream_t st) {
   const BandGeom& G = geom();
   const int T = e->cur_T;
+  if (e->cur_B != 1) return fail(LBRR_ERR_STATE, "the per-stem back end takes one chunk");
   const int per = e->n_m2 / kStems;
   const size_t chan = static_cast<size_t>(len);
   for (int s = 0; s < kStems; ++s) {
     CKL(gemm_mask2(e->hidden, e->mask_w2, e->mask_b2, e->band_f0, e->band_d, e->band_o2, e->spec, e->c2r, T, kStems,
                    G.n2tot, e->tiles_m2 + s * per, per, e->keep_dc_imag, e->status, st));
     CKL(istft_back(e->c2r + static_cast<size_t>(2 * s) * T * kBins, e->window, e->twiddles, e->inv_env,
-                   e->dev_out + 2 * s * chan, static_cast<int>(len), T, 2, st));
+                   e->dev_out + 2 * s * chan, static_cast<int>(len), T, 2, 1, st));
     CK(cudaEventRecord(e->stem_ev[s], st));
     CK(cudaStreamWaitEvent(e->host_copy, e->stem_ev[s], 0));
     CK(cudaMemcpyAsync(outh + 2 * s * chan, e->dev_out + 2 * s * chan, 2 * chan * sizeof(float),
@@ -1059,20 +1082,21 @@ static int capture_forward(lbrr_engine* e, const float* x, int64_t len, float* o
   return e->graph ? LBRR_OK : LBRR_ERR_CUDA;
 }
 
-extern "C" int lbrr_forward_chunk(lbrr_engine* e, const float* x, int64_t len, float* out, void* stream) {
-  if (int rc = check_forward_args(e, x, len, out)) return rc;
-  DeviceGuard g(e->device);
-  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
-  if (int rc = setup_length(e, len)) return rc;
+// B chunks of len samples (x: B x [len][2], out: B x [6][2][len]) in one
+// forward, replayed as a CUDA graph for the same (x, out, len, B, stream) on
+// the second call in a row.
+static int forward_device(lbrr_engine* e, const float* x, int64_t len, int B, float* out, cudaStream_t st) {
+  if (int rc = setup_length(e, len, B)) return rc;
   const bool capturable = st != cudaStreamLegacy && st != cudaStreamPerThread && st != nullptr;
   if (capturable) {
-    if (e->graph && e->graph_x == x && e->graph_out == out && e->graph_len == len && e->graph_stream == st) {
+    const bool same = e->graph_x == x && e->graph_out == out && e->graph_len == len && e->graph_B == B &&
+                      e->graph_stream == st;
+    if (e->graph && same) {
       CK(cudaGraphLaunch(e->graph, st));
       return LBRR_OK;
     }
     // capture on the second consecutive call with the same buffers: the first
     // one runs directly and performs every one-time setup outside a capture
-    const bool same = e->graph_x == x && e->graph_out == out && e->graph_len == len && e->graph_stream == st;
     if (e->graph) cudaGraphExecDestroy(e->graph);
     e->graph = nullptr;
     if (same && e->graph_seen >= 1 && capture_forward(e, x, len, out, st) == LBRR_OK) {
@@ -1083,9 +1107,33 @@ extern "C" int lbrr_forward_chunk(lbrr_engine* e, const float* x, int64_t len, f
     e->graph_x = x;
     e->graph_out = out;
     e->graph_len = len;
+    e->graph_B = B;
     e->graph_stream = st;
   }
   return run_forward(e, x, len, out, st);
+}
+
+extern "C" int lbrr_forward_chunk(lbrr_engine* e, const float* x, int64_t len, float* out, void* stream) {
+  if (int rc = check_forward_args(e, x, len, out)) return rc;
+  DeviceGuard g(e->device);
+  return forward_device(e, x, len, 1, out, stream ? static_cast<cudaStream_t>(stream) : e->stream);
+}
+
+extern "C" int lbrr_forward_chunks(lbrr_engine* e, const float* x, int64_t len, int32_t n_chunks, float* out,
+                                   void* stream) {
+  if (int rc = check_forward_args(e, x, len, out)) return rc;
+  if (n_chunks < 1) return fail(LBRR_ERR_INVALID, "n_chunks must be >= 1");
+  if (static_cast<int64_t>(n_chunks) * T_of(len) > e->max_T)
+    return fail(LBRR_ERR_INVALID, "n_chunks * (len / 512 + 1) frames exceed the engine's max_chunk_samples / 512 + 1");
+  DeviceGuard g(e->device);
+  cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
+  if (n_chunks == 1 || use_cufft_front(e) || use_cufft_back(e)) {
+    // the cuFFT paths take one chunk per forward
+    for (int c = 0; c < n_chunks; ++c)
+      if (int rc = forward_device(e, x + 2 * c * len, len, 1, out + 2 * kStems * c * len, st)) return rc;
+    return LBRR_OK;
+  }
+  return forward_device(e, x, len, n_chunks, out, st);
 }
 
 extern "C" int lbrr_forward_trunk(lbrr_engine* e, const float* x, int64_t len, int n_steps, float* x_out,
@@ -1098,7 +1146,8 @@ extern "C" int lbrr_forward_trunk(lbrr_engine* e, const float* x, int64_t len, i
   if (int rc = run_front(e, x, len, st)) return rc;
   for (int k = 0; k < n_steps; ++k)
     if (int rc = run_step(e, k, st)) return rc;
-  CK(cudaMemcpyAsync(x_out, e->x, static_cast<size_t>(e->cur_T) * kNumBands * 256 * 4, cudaMemcpyDeviceToDevice, st));
+  CK(cudaMemcpyAsync(x_out, e->x, static_cast<size_t>(frames_all(e)) * kNumBands * 256 * 4, cudaMemcpyDeviceToDevice,
+                     st));
   return LBRR_OK;
 }
 
@@ -1106,6 +1155,7 @@ extern "C" int lbrr_forward_back(lbrr_engine* e, int64_t len, float* stems_dev, 
   if (!e || !stems_dev) return fail(LBRR_ERR_INVALID, "NULL argument");
   if (e->cur_len <= 0) return fail(LBRR_ERR_STATE, "no forward has run yet");
   if (len != e->cur_len) return fail(LBRR_ERR_STATE, "len differs from the last forward's");
+  if (e->cur_B != 1) return fail(LBRR_ERR_STATE, "the last forward was a batch of chunks");
   DeviceGuard g(e->device);
   cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e->stream;
   return run_back(e, len, stems_dev, st);
@@ -1129,7 +1179,7 @@ extern "C" int lbrr_engine_read_buffer(lbrr_engine* e, const char* name, void* d
   if (!e || !name || !dst || bytes < 0) return fail(LBRR_ERR_INVALID, "NULL argument");
   if (e->cur_T <= 0) return fail(LBRR_ERR_STATE, "no forward has run yet");
   DeviceGuard g(e->device);
-  const size_t T = e->cur_T, M = T * kNumBands;
+  const size_t T = frames_all(e), M = T * kNumBands;
   const void* src = nullptr;
   size_t cap = 0;
   const std::string n(name);
@@ -1946,7 +1996,7 @@ extern "C" int lbrr_op_attention(const uint16_t* qkv, const float* gates, uint16
     return fail(LBRR_ERR_INVALID, "lbrr_op_attention: bad arguments (freq axis needs bands <= 64)");
   OP_PROLOGUE
   CK(attention_fwd(reinterpret_cast<const __half*>(qkv), gates, reinterpret_cast<__half*>(out),
-                   static_cast<int>(frames), bands, axis, status, st));
+                   static_cast<int>(frames), bands, axis, 1, status, st));
   return LBRR_OK;
 }
 

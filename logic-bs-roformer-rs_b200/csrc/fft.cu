@@ -153,7 +153,13 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
   float2* tw = fsm + 2 * kXpose;
   int* stab = reinterpret_cast<int*>(tw + kTwS);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // frame t of chunk blockIdx.y: that chunk's samples start len stereo pairs
+  // further on; its frames are rows chunk*T.. of the chunks' common spectrum
+  // planes (T * gridDim.y frames per channel) and band-split rows
   const int t = blockIdx.x;
+  const int tg = blockIdx.y * T + t;
+  const int Tp = T * gridDim.y;
+  x += 2ll * len * blockIdx.y;
   const int pad = kNfft / 2;
   // Interior frames (no reflection) stage their 2048 interleaved stereo
   // samples, 16 KB contiguous and 16-byte aligned, with coalesced 16-byte loads
@@ -218,7 +224,7 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
       }
     }
     __syncwarp();
-    float2* out = spec + (static_cast<size_t>(ch) * T + t) * kBins;
+    float2* out = spec + (static_cast<size_t>(ch) * Tp + tg) * kBins;
     for (int k = lane; k < kBins; k += 32) out[k] = xp[k];
   }
   __syncthreads();
@@ -239,7 +245,7 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
     }
     ss = warp_sum(ss);
     const float scale = sqrtf(static_cast<float>(d)) / fmaxf(sqrtf(ss), 1e-12f);
-    __half2* row = reinterpret_cast<__half2*>(xn + static_cast<long long>(t) * xn_cols + koff);
+    __half2* row = reinterpret_cast<__half2*>(xn + static_cast<long long>(tg) * xn_cols + koff);
     for (int j = 2 * lane; j < kpad; j += 64) {
       const float a0 = j < d ? __fmul_rn(__fmul_rn(value(j), scale), __ldg(gamma + goff + j)) : 0.f;
       const float a1 = j + 1 < d ? __fmul_rn(__fmul_rn(value(j + 1), scale), __ldg(gamma + goff + j + 1)) : 0.f;
@@ -249,11 +255,13 @@ __global__ void __launch_bounds__(kFrontWarps * 32, 5) stft_front_kernel(const f
 }
 
 cudaError_t stft_front(const float* x, const float* window, const float2* twiddles, float2* spec, const float* gamma,
-                       const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb, cudaStream_t st) {
+                       const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb, int chunks,
+                       cudaStream_t st) {
   if ((xn_cols & 1) != 0 || nb > kNumBands) return cudaErrorInvalidValue;  // half2 row stores, table size
+  if (chunks < 1 || chunks > 65535) return cudaErrorInvalidValue;
   count_launch();
-  stft_front_kernel<<<T, kFrontWarps * 32, kFrontSmem, st>>>(x, window, twiddles, spec, gamma, band_tab, xn,
-                                                             xn_cols, len, T, nb);
+  stft_front_kernel<<<dim3(T, chunks), kFrontWarps * 32, kFrontSmem, st>>>(x, window, twiddles, spec, gamma, band_tab,
+                                                                          xn, xn_cols, len, T, nb);
   return cudaGetLastError();
 }
 
@@ -277,7 +285,10 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
   extern __shared__ __align__(16) float2 bsm[];
   float2* tw = bsm + kBackWarps * kXpose;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // channel sc of chunk blockIdx.z: frames chunk*T.. of the chunks' common
+  // spectrum planes (T * gridDim.z frames each), samples into out[chunk][sc]
   const int sc = blockIdx.y;
+  const int Tp = T * gridDim.z;
   const int k0 = 2 + blockIdx.x * kBackBlocks;
   const int t = k0 - 3 + warp;
   const bool has_frame = t >= 0 && t < T;
@@ -286,7 +297,7 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
   if (has_frame) {
     // the frame's 1025 bins into its slot with coalesced 16-byte loads: the
     // 16-byte-aligned span holding them (at most 8 bytes before and after)
-    const float2* X = c2r + (static_cast<size_t>(sc) * T + t) * kBins;
+    const float2* X = c2r + (static_cast<size_t>(sc) * Tp + static_cast<size_t>(blockIdx.z) * T + t) * kBins;
     shift = static_cast<int>((reinterpret_cast<uintptr_t>(X) >> 3) & 1);
     const float4* src = reinterpret_cast<const float4*>(X - shift);
     float4* dst = reinterpret_cast<float4*>(xp);
@@ -329,7 +340,7 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
   __syncthreads();
   // overlap-add in frame order, envelope, crop to [n_fft/2, n_fft/2 + len)
   const int p_lo = max(k0 * kHop, kNfft / 2), p_hi = min((k0 + kBackBlocks) * kHop, kNfft / 2 + len);
-  float* o = out + static_cast<size_t>(sc) * len;
+  float* o = out + (static_cast<size_t>(blockIdx.z) * gridDim.y + sc) * len;
   for (int p = p_lo + threadIdx.x; p < p_hi; p += blockDim.x) {
     const int k = p / kHop;
     float sum = 0.f;
@@ -345,7 +356,7 @@ __global__ void __launch_bounds__(kBackWarps * 32, 2) istft_back_kernel(const fl
 }
 
 cudaError_t istft_back(const float2* c2r, const float* window, const float2* twiddles, const float* inv_env,
-                       float* out, int len, int T, int channels, cudaStream_t st) {
+                       float* out, int len, int T, int channels, int chunks, cudaStream_t st) {
   static unsigned long long configured = 0;
   cudaError_t e = once_per_device(configured, [] {
     cudaError_t r = cudaFuncSetAttribute(istft_back_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kBackSmem);
@@ -357,9 +368,10 @@ cudaError_t istft_back(const float2* c2r, const float* window, const float2* twi
   if (e != cudaSuccess) return e;
   const int k_last = (len + kNfft / 2 - 1) / kHop;  // last output block
   const int groups = (k_last - 2 + 1 + kBackBlocks - 1) / kBackBlocks;
+  if (chunks < 1 || chunks > 65535) return cudaErrorInvalidValue;
   count_launch();
-  istft_back_kernel<<<dim3(groups, channels), kBackWarps * 32, kBackSmem, st>>>(c2r, window, twiddles, inv_env, out,
-                                                                                 len, T);
+  istft_back_kernel<<<dim3(groups, channels, chunks), kBackWarps * 32, kBackSmem, st>>>(c2r, window, twiddles,
+                                                                                         inv_env, out, len, T);
   return cudaGetLastError();
 }
 

@@ -81,8 +81,10 @@ cudaError_t gemm_mask2(const __half* hidden, const __half* w2, const float* b2, 
                        cudaStream_t st);
 
 // ---- attention (attention.cu) ----------------------------------------------
-cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int* status,
-                          cudaStream_t st);
+// chunks: forwards batched along the frame axis (chunk c at frames c*T..);
+// the time axis keeps their frames apart, the frequency axis sees T * chunks frames
+cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, int T, int nb, int axis, int chunks,
+                          int* status, cudaStream_t st);
 
 // ---- bandwidth kernels (spectral.cu) ---------------------------------------
 cudaError_t stft_frames(const float* x_interleaved, const float* window, float* frames, int len, int T,
@@ -96,11 +98,15 @@ cudaError_t istft_ola(const float* pcm, const float* window, const float* inv_en
 
 // ---- in-house FFT, fused with its neighbours (fft.cu) ------------------------
 // twiddles: [2048] exp(+2 pi i k / 2048) as float2
+// chunks: x holds `chunks` interleaved inputs of len samples one after another;
+// chunk c's frames are rows c*T.. of the spectrum planes ([2][T*chunks][1025])
+// and of xn
 cudaError_t stft_front(const float* x_interleaved, const float* window, const float2* twiddles, float2* spec,
                        const float* gamma, const int* band_tab, __half* xn, int xn_cols, int len, int T, int nb,
-                       cudaStream_t st);
+                       int chunks, cudaStream_t st);
+// c2r planes [channels][T*chunks][1025] -> out [chunks][channels][len]
 cudaError_t istft_back(const float2* c2r, const float* window, const float2* twiddles, const float* inv_env,
-                       float* out, int len, int T, int channels, cudaStream_t st);
+                       float* out, int len, int T, int channels, int chunks, cudaStream_t st);
 
 // cudaFuncSetAttribute (the dynamic shared-memory opt-in) acts on the current
 // device only.  Runs `setup` once per device (devices 0..63, bit d of `done`)

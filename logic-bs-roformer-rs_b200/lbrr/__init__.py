@@ -80,6 +80,7 @@ def lib() -> C.CDLL:
         "lbrr_check_weights": ([C.POINTER(WeightView), C.c_size_t], C.c_int),
         "lbrr_check_safetensors": ([C.c_char_p], C.c_int),
         "lbrr_forward_chunk": ([vp, vp, i64, vp, vp], C.c_int),
+        "lbrr_forward_chunks": ([vp, vp, i64, i32, vp, vp], C.c_int),
         "lbrr_forward_chunk_host": ([vp, vp, i64, vp], C.c_int),
         "lbrr_forward_trunk": ([vp, vp, i64, C.c_int, vp, vp], C.c_int),
         "lbrr_forward_back": ([vp, i64, vp, vp], C.c_int),
@@ -113,7 +114,7 @@ def lib() -> C.CDLL:
 # Every symbol include/lbrr_gpu.h declares (checked by the CPU test suite).
 HEADER_SYMBOLS = [
     "lbrr_last_error", "lbrr_abi_version", "lbrr_host_alloc", "lbrr_host_free", "lbrr_default_model", "lbrr_engine_create", "lbrr_engine_load_weights",
-    "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
+    "lbrr_engine_load_safetensors", "lbrr_check_weights", "lbrr_check_safetensors", "lbrr_forward_chunk", "lbrr_forward_chunks", "lbrr_forward_chunk_host", "lbrr_forward_trunk",
     "lbrr_forward_back",
     "lbrr_engine_sync", "lbrr_engine_set_option", "lbrr_engine_get_option", "lbrr_engine_wait_probe",
     "lbrr_engine_read_buffer", "lbrr_engine_memory", "lbrr_engine_destroy", "lbrr_separate_song", "lbrr_op_norm_gates",
@@ -217,6 +218,13 @@ class Engine:
         """One chunk on device buffers: x [len][2] fp32 -> stems [6][2][len] fp32."""
         length = x_dev.numel() // 2
         check(lib().lbrr_forward_chunk(self.handle, _ptr(x_dev), length, _ptr(out_dev), _stream(stream)))
+
+    def forward_chunks(self, x_dev, out_dev, stream=None):
+        """Chunks of equal length batched in one forward: x [n][len][2] fp32 ->
+        stems [n][6][2][len] fp32, each chunk bit-identical to bench_forward on it."""
+        n = x_dev.shape[0]
+        length = x_dev.numel() // (2 * n)
+        check(lib().lbrr_forward_chunks(self.handle, _ptr(x_dev), length, n, _ptr(out_dev), _stream(stream)))
 
     def forward_host(self, x_host: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
         """End to end from host memory: x [len][2] fp32 -> stems [6][2][len] fp32
