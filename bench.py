@@ -427,8 +427,22 @@ def time_batched_chunks(torch, lbrr, local_rank, stream, flush, args):
         ms = _time_steps(torch, lambda: eb.forward_chunks(x2, out2, stream=stream), stream, flush,
                          min(args.steps, 10), 3)
         eb.sync()
-        return {"ms_per_chunk": round(ms / 2, 4), "ms_per_batch": round(ms, 4), "chunks": 2,
-                "how": "lbrr_forward_chunks: both chunks' frames in every launch (2 x 1151 frames), graph replay"}
+        res = {"ms_per_chunk": round(ms / 2, 4), "ms_per_batch": round(ms, 4), "chunks": 2,
+               "how": "lbrr_forward_chunks: both chunks' frames in every launch (2 x 1151 frames), graph replay"}
+        del x2, out2
+        # the 132300-sample chunk (T = 259): one chunk's 126 row tiles leave 22 of 148 SMs idle
+        L = 132300
+        short = {}
+        for n in (1, 2, 4, 7):
+            xs = torch.from_numpy(np.stack([np.ascontiguousarray(synthetic.audio(L, seed=s).T)
+                                            for s in range(n)])).cuda()
+            outs = torch.empty(n, 6, 2, L, device="cuda")
+            ms = _time_steps(torch, lambda: eb.forward_chunks(xs, outs, stream=stream), stream, flush,
+                             min(args.steps, 10), 3)
+            eb.sync()
+            short[str(n)] = round(ms / n, 4)
+        res["short_chunk_ms_per_chunk"] = short
+        return res
     finally:
         eb.close()
 
