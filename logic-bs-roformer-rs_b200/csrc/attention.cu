@@ -57,9 +57,9 @@ __device__ __forceinline__ float ex2(float x) {
 // columns, right after O += P(j)·V(j) (TS form, A = P from TMEM).  The
 // softmax warpgroup takes 224 registers per thread from warpgroup 1
 // (setmaxnreg), enough for a whole S row and its fp16 P without spilling.
-// Chunks batched into one forward are grid.z: chunk c's frames are rows
-// c*T.. of the frame axis; the key rows past its T valid frames (the next
-// chunk's, or the tensor map's zero fill after the last chunk) are masked.
+// Chunks batched into one forward are grid.z and the 4th coordinate of the
+// tensor map ([chunk][T][nb][1536]): key rows past a chunk's T frames are the
+// map's zero fill, as for a single chunk, and are masked.
 constexpr int kT1Threads = 256;
 constexpr int kT1WarpTma = 4, kT1WarpMma = 5;
 constexpr int kT1RegsSoftmax = 224, kT1RegsOther = 32;
@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(kT1Threads, 2)
   const int nb = a.nb, T = a.T, nk = a.nk;
   const int head = blockIdx.y & 7, band = blockIdx.y >> 3;
   const int qt = blockIdx.x;
-  const int t0 = blockIdx.z * T;  // this chunk's first frame
+  const int chunk = blockIdx.z;
+  const int t0 = chunk * T;  // this chunk's first frame
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -130,14 +131,14 @@ __global__ void __launch_bounds__(kT1Threads, 2)
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, kTile);
-      tma_load_3d(smem + kT1OffQ, &tm, q_full, head * 64, band, t0 + qt * 128);
+      tma_load_4d(smem + kT1OffQ, &tm, q_full, head * 64, band, qt * 128, chunk);
       for (int j = 0; j < nk; ++j) {
         const int st = j % kT1Stages;
         if (!mbar_wait(&kv_empty[st], ((j / kT1Stages) & 1) ^ 1u, abort_flag, a.status)) break;
         mbar_arrive_expect_tx(&kv_full[st], 2 * kTile);
         uint8_t* kv = smem + kT1OffKV + st * 2 * kTile;
-        tma_load_3d(kv, &tm, &kv_full[st], 512 + head * 64, band, t0 + j * 128);
-        tma_load_3d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, t0 + j * 128);
+        tma_load_4d(kv, &tm, &kv_full[st], 512 + head * 64, band, j * 128, chunk);
+        tma_load_4d(kv + kTile, &tm, &kv_full[st], 1024 + head * 64, band, j * 128, chunk);
       }
     }
   } else if (warp == kT1WarpMma) {
@@ -354,6 +355,10 @@ __global__ void __launch_bounds__(kT1Threads, 2)
 // during that item's epilogue) and O = P V once P is written and the previous
 // output has left TMEM, warps 2..5 run the softmax (one row per thread, only the
 // row's own sequence as keys) and the epilogue f16(f16(O/l) * sigmoid(gate)).
+// Chunks batched into one forward are the 3rd coordinate of the tensor map
+// ([chunk][T*nb][1536]) and pair frames only within themselves: with T odd the
+// last item of a chunk holds one frame and the map's zero fill, as for a
+// single chunk, so no item ever mixes two chunks' values.
 constexpr int kFStages = 2;
 constexpr int kFStage = 3 * kTile;  // Q, K, V
 constexpr int kFOffBar = kFStages * kFStage;
@@ -379,6 +384,7 @@ __global__ void __launch_bounds__(kFThreads, 2)
     return;
   }
   const int nb = a.nb, T = a.T;
+  const int pairs = (T + 1) / 2;  // items per head and chunk
   if (threadIdx.x == 0) {
     for (int i = 0; i < kFStages; ++i) {
       mbar_init(&full[i], 1);
@@ -417,12 +423,12 @@ __global__ void __launch_bounds__(kFThreads, 2)
       for (int it = blockIdx.x; it < n_items; it += gridDim.x, ++k) {
         const int st = k & 1;
         if (!mbar_wait(&empty[st], ((k >> 1) & 1) ^ 1u, abort_flag, a.status)) break;
-        const int head = it & 7, row0 = (it >> 3) * 2 * nb;
+        const int head = it & 7, chunk = (it >> 3) / pairs, row0 = ((it >> 3) - chunk * pairs) * 2 * nb;
         uint8_t* s = smem + st * kFStage;
         mbar_arrive_expect_tx(&full[st], 3 * 2 * nb * 128);
         for (int h = 0; h < 2; ++h)
           for (int m = 0; m < 3; ++m)
-            tma_load_2d(s + m * kTile + h * 64 * 128, &tm, &full[st], m * 512 + head * 64, row0 + h * nb);
+            tma_load_3d(s + m * kTile + h * 64 * 128, &tm, &full[st], m * 512 + head * 64, row0 + h * nb, chunk);
       }
     }
   } else if (warp == 1) {
@@ -472,9 +478,9 @@ __global__ void __launch_bounds__(kFThreads, 2)
     bool ok = true;
     int k = 0;
     for (int it = blockIdx.x; ok && it < n_items; it += gridDim.x, ++k) {
-      const int head = it & 7, t = (it >> 3) * 2 + rseq;
+      const int head = it & 7, chunk = (it >> 3) / pairs, t = ((it >> 3) - chunk * pairs) * 2 + rseq;
       const bool valid = ri < nb && t < T;
-      const int token = t * nb + ri;
+      const int token = (chunk * T + t) * nb + ri;
       // the gate is independent of the MMAs: fetch it before waiting
       const float gate = valid ? __ldg(a.gates + static_cast<size_t>(token) * 8 + head) : 0.f;
       ok = mbar_wait(s_full, k & 1, abort_flag, a.status);
@@ -589,8 +595,12 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
   a.axis = axis;
   a.status = status;
   if (axis == 0) {
-    e = make_map_3d(&tm, qkv, 1536, nb, static_cast<uint64_t>(T) * chunks, 1536 * 2,
-                    static_cast<uint64_t>(nb) * 1536 * 2, 64, 1, 128);
+    const uint64_t dims[4] = {1536, static_cast<uint64_t>(nb), static_cast<uint64_t>(T),
+                              static_cast<uint64_t>(chunks)};
+    const uint64_t strides[3] = {1536 * 2, static_cast<uint64_t>(nb) * 1536 * 2,
+                                 static_cast<uint64_t>(T) * nb * 1536 * 2};
+    const uint32_t box[4] = {64, 1, 128, 1};
+    e = make_map_4d(&tm, qkv, dims, strides, box);
     if (e != cudaSuccess) return e;
     a.nk = (T + 127) / 128;
     // one query tile per CTA, two CTAs per SM
@@ -598,15 +608,13 @@ cudaError_t attention_fwd(const __half* qkv, const float* gates, __half* out, in
     attn_time_kernel<<<dim3(a.nk, nb * 8, chunks), kT1Threads, kT1Smem, st>>>(tm, a);
     return cudaGetLastError();
   }
-  // frequency axis: every frame of every chunk is one sequence
-  T *= chunks;
-  a.T = T;
-  // boxes of one frame's nb tokens
-  e = make_map_2d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, 1536 * 2, 64, nb);
+  // boxes of one frame's nb tokens, [chunk][T * nb][1536]
+  e = make_map_3d(&tm, qkv, 1536, static_cast<uint64_t>(T) * nb, chunks, 1536 * 2,
+                  static_cast<uint64_t>(T) * nb * 1536 * 2, 64, nb, 1);
   if (e != cudaSuccess) return e;
   a.nk = 1;
-  // (frame pair, head) items over two persistent CTAs per SM
-  const int n_items = (T + 1) / 2 * 8;
+  // (chunk, frame pair, head) items over two persistent CTAs per SM
+  const int n_items = chunks * ((T + 1) / 2) * 8;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);

@@ -57,6 +57,9 @@ cudaError_t make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint
 cudaError_t make_map_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1_bytes,
                         uint64_t s2_bytes, uint32_t b0, uint32_t b1, uint32_t b2, MapElem elem = MapElem::F16,
                         CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
+// fp16, 128-byte swizzle
+cudaError_t make_map_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t stride_bytes[3],
+                        const uint32_t box[4]);
 
 // ---- GEMMs (gemm.cu) -------------------------------------------------------
 cudaError_t gemm_qkv(const __half* h16, const __half* w, const float* bias16, const float* cos, const float* sin,

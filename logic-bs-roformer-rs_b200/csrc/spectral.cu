@@ -65,6 +65,27 @@ cudaError_t make_map_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
+cudaError_t make_map_4d(CUtensorMap* map, const void* base, const uint64_t dims[4], const uint64_t stride_bytes[3],
+                        const uint32_t box[4]) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return cudaErrorNotSupported;
+  if (reinterpret_cast<uintptr_t>(base) & 15u) return cudaErrorMisalignedAddress;
+  cuuint64_t d[4], s[3];
+  cuuint32_t b[4], estr[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 4; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i < 3; ++i) {
+    if (stride_bytes[i] & 15u) return cudaErrorMisalignedAddress;
+    s[i] = stride_bytes[i];
+  }
+  CUresult r = fn(map, map_dtype(MapElem::F16), 4, const_cast<void*>(base), d, s, b, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
 // ---------------------------------------------------------------------------
 // STFT framing: frames[ch][t][j] = x[src][ch] * window[j] with torch/numpy
 // reflect padding of n_fft/2 (frame_hann_reflect, src/main.rs:396-429).

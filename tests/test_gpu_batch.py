@@ -107,3 +107,24 @@ def test_batched_chunks_cufft_backend_and_limits(engine):
     assert ei.value.code == lbrr.ERR_INVALID
     again = _singles(engine, x)
     assert torch.equal(again, base)
+
+
+def test_batched_chunks_stay_apart_when_one_is_not_finite(engine):
+    """A chunk whose samples hold NaN (data only: no index in the forward
+    depends on a value) poisons its own stems and nothing else: both
+    attention kernels read each chunk through its own coordinate of the
+    tensor map, so the rows past a chunk's last frame are zero fill, never the
+    next chunk's keys and values.  T = 41 is odd: the frequency axis's last
+    frame pair of each chunk holds one frame (and would hold the next chunk's
+    first frame if frames were paired across chunks)."""
+    L, B = 20480, 3
+    _, x = _chunks(L, B, seed=110)
+    x[1, 5000:5100] = float("nan")
+    ref = _singles(engine, x)
+    out = torch.empty(B, 6, 2, L, device="cuda")
+    engine.forward_chunks(x, out)
+    engine.sync()
+    assert torch.isnan(out[1]).any()
+    for b in (0, 2):
+        assert torch.isfinite(out[b]).all()
+        assert torch.equal(out[b], ref[b]), b
